@@ -1,0 +1,440 @@
+#!/usr/bin/env python
+"""Benchmark of the 2-bit MoE gather-GEMV path (BASELINE.json metric).
+
+One *step* is one token (M=1, config 1) or one verify batch (M=8, config 2)
+through 48 MoE layers with distinct weights: per layer the router top-k,
+up||gate gather-GEMV + SwiGLU, down gather-GEMV, score-weighted combine into
+the residual stream (h += MoE(h)).  Weights are generated on the GPU from the
+seeded generator (36 GB for config 1), so every step streams ~2.3 GB of
+distinct expert weights: inputs larger than L2, no flush needed.
+
+Timing: W untimed steps, then K steps replayed from one CUDA graph, bracketed
+by a barrier + synchronize, CUDA events on the launching stream, max over
+ranks.  `e2e` repeats the K steps through the public API with the step's
+inputs copied from pinned host memory and the output read back inside the
+timed region.  With --gpus N>1 each rank runs an independent replica
+(weak scaling, no collective on the data path).
+
+`--impl reference` times the CPU restatement of the reference's path
+(oracle/, OpenMP over all host cores) on rank 0: the reference itself is
+Swift + Metal + MLX and cannot run on this box.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    "decode": dict(desc="BASELINE config 1: decode M=1, H=4096, E=128, top-8, I=1536, gs64, "
+                        "48 layers with distinct weights", H=4096, I=1536, E=128, K=8, gs=64, M=1,
+                   L=48, rho=None),
+    "verify": dict(desc="BASELINE config 2: verify batch M=8 (rho=0.7 correlated logits), "
+                        "config-1 shapes, 48 layers", H=4096, I=1536, E=128, K=8, gs=64, M=8,
+                   L=48, rho=0.7),
+}
+METRIC = "2-bit MoE gather-GEMV tokens/s"
+
+
+def load_peaks() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except Exception:
+            pass
+        finally:
+            try:
+                os.unlink(self.path)
+            except Exception:
+                pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]
+                          and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_setup():
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------
+# CPU leg: the oracle (CPU restatement of the reference path), all host cores
+# ---------------------------------------------------------------------------
+
+def cpu_layer_sample(cfg: dict, wh: dict, x: np.ndarray, inds: np.ndarray, scores: np.ndarray,
+                     budget_s: float) -> dict:
+    """Times oracle.expert_ffn on one layer's selected experts for ~budget_s."""
+    from oracle import oracle as O
+    M, H, I, K, gs = cfg["M"], cfg["H"], cfg["I"], cfg["K"], cfg["gs"]
+    O.expert_ffn(x, wh, inds, scores, M, H, I, K, gs)  # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        O.expert_ffn(x, wh, inds, scores, M, H, I, K, gs)
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = (time.perf_counter() - t0) / n
+    tok_s = M / (dt * cfg["L"])
+    return {"value": tok_s, "unit": "tokens/s", "cores": O.num_threads(), "kind": "port",
+            "sample": f"{n} evaluations of one layer's expert FFN ({cfg['M']} token(s), "
+                      f"{len(np.unique(inds))} experts, {dt * 1e3:.1f} ms each); tokens/s scaled to "
+                      f"{cfg['L']} layers",
+            "layer_ms": dt * 1e3}
+
+
+def host_layer_inputs(cfg: dict, layer: int = 0):
+    """Host copies of one layer's inputs for the CPU leg (selected experts only)."""
+    import torch
+    from momij_b200 import moe, synth as S
+    H, I, E, K, gs, M = (cfg[k] for k in ("H", "I", "E", "K", "gs", "M"))
+    lg = (S.logits_ar1(M, E, cfg["rho"], layer, 0) if cfg["rho"]
+          else S.logits_normal(M, E, layer, 0))
+    from oracle import oracle as O
+    inds, scores = O.route(lg, K)
+    uniq, remap = np.unique(inds, return_inverse=True)
+    wd = moe.device_expert_weights(E, H, I, gs, layer=layer, seed=0)
+    idx = torch.from_numpy(uniq.astype(np.int64)).cuda()
+    wh = {k: v.index_select(0, idx).view(torch.int32 if k.startswith("w_") else torch.int16)
+          .cpu().numpy().view(np.uint32 if k.startswith("w_") else np.uint16) for k, v in wd.items()}
+    del wd
+    x = S.activations(M, H, layer, 0)
+    return wh, x, remap.reshape(M, K).astype(np.int32), scores
+
+
+def run_reference(args, cfg) -> None:
+    world, rank, _ = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
+    if rank != 0:
+        return
+    from momij_b200 import synth as S
+    from oracle import oracle as O
+    H, I, E, K, gs, M = (cfg[k] for k in ("H", "I", "E", "K", "gs", "M"))
+    # The CPU leg needs no GPU: generate the selected experts' weights on the host.
+    lg = (S.logits_ar1(M, E, cfg["rho"], 0, 0) if cfg["rho"] else S.logits_normal(M, E, 0, 0))
+    inds, scores = O.route(lg, K)
+    uniq, remap = np.unique(inds, return_inverse=True)
+    full = {}
+    for k, kind, shape in (("w_ug", S.KIND_W_UG, (2 * I, H // 16)), ("w_dn", S.KIND_W_DN, (H, I // 16))):
+        n = shape[0] * shape[1]
+        full[k] = np.stack([S.codes(n, 0, S.stream_id(0, kind), int(e) * n).reshape(shape) for e in uniq])
+    for k, kind, shape, a, c in (("s_ug", S.KIND_S_UG, (2 * I, H // gs), S.SCALE_A, S.SCALE_C),
+                                 ("b_ug", S.KIND_B_UG, (2 * I, H // gs), S.BIAS_A, S.BIAS_C),
+                                 ("s_dn", S.KIND_S_DN, (H, I // gs), S.SCALE_A, S.SCALE_C),
+                                 ("b_dn", S.KIND_B_DN, (H, I // gs), S.BIAS_A, S.BIAS_C)):
+        n = shape[0] * shape[1]
+        full[k] = np.stack([S.affine_uniform(n, a, c, 0, S.stream_id(0, kind), 0, int(e) * n)
+                            .reshape(shape) for e in uniq])
+    x = S.activations(M, H, 0, 0)
+    rinds = remap.reshape(M, K).astype(np.int32)
+    for _ in range(args.warmup):
+        O.expert_ffn(x, full, rinds, scores, M, H, I, K, gs)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.expert_ffn(x, full, rinds, scores, M, H, I, K, gs)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    tok_s = M / (dt * cfg["L"])
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tok_s, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": cfg["desc"], "H": H, "E": E, "top_k": K, "I": I, "gs": gs, "M": M,
+                   "layers": cfg["L"], "parallelism": "cpu"},
+        "cpu_baseline": {"value": tok_s, "unit": "tokens/s", "cores": O.num_threads(),
+                         "kind": "port",
+                         "sample": f"each step = one layer's expert FFN ({M} token(s), {len(uniq)} "
+                                   f"experts) on the host; tokens/s scaled to {cfg['L']} layers. "
+                                   "The reference (Swift/Metal/MLX) cannot run here; this is the "
+                                   "oracle's CPU restatement of its path."},
+        "e2e": {"value": tok_s, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+# ---------------------------------------------------------------------------
+
+def run_gpu(args, cfg) -> None:
+    import torch
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    from momij_b200 import moe, synth as S
+
+    H, I, E, K, gs, M, L = (cfg[k] for k in ("H", "I", "E", "K", "gs", "M", "L"))
+    P = M * K
+    dev = torch.device("cuda", local)
+    W = [moe.device_expert_weights(E, H, I, gs, layer=l, seed=0, device=dev) for l in range(L)]
+    lg_host = np.stack([(S.logits_ar1(M, E, cfg["rho"], l, 0) if cfg["rho"]
+                         else S.logits_normal(M, E, l, 0)) for l in range(L)])
+    x_host = S.activations(M, H, 0, 0)
+    logits = torch.from_numpy(lg_host).to(dev)
+    h0 = torch.from_numpy(x_host.view(np.int16)).to(dev).view(torch.bfloat16)
+    h = h0.clone()
+    ws = moe.new_workspace(M, K, H, I, dev)
+    inds_all = torch.empty(L, M, K, dtype=torch.int32, device=dev)
+    scores_all = torch.empty(L, M, K, dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    # algorithmic bytes: the distinct experts each layer streams
+    eb = S.expert_bytes(H, I, gs)
+    up_bytes = (2 * I) * (H // 16) * 4 + (2 * I) * (H // gs) * 4
+    dn_bytes = eb - up_bytes
+
+    def step():
+        for l in range(L):
+            moe.forward(logits[l], h, W[l], None, H=H, I=I, Ktop=K, gs=gs, M=M, inds=inds_all[l],
+                        scores=scores_all[l], resid_h=h, workspace=ws, stream=stream)
+
+    # eager warm-up (also validates the status once)
+    with torch.cuda.stream(stream):
+        step()
+    moe.synchronize(stream, ws)
+    # algorithmic bytes: the distinct experts each layer streams (from the
+    # router outputs the GPU itself produced)
+    ih = inds_all.cpu().numpy()
+    uniq = [len(np.unique(ih[l])) for l in range(L)]
+    bytes_per_step = sum(uniq) * eb
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    torch.cuda.synchronize()
+
+    # CUDAGraph.replay() launches on the *current* stream: keep it `stream`,
+    # the stream the timing events are recorded on.
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            graph.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        barrier(world)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            ev1.record(stream)
+        torch.cuda.synchronize()
+    dev_ms = ev0.elapsed_time(ev1)
+    barrier(world)
+    dev_ms = max_over_ranks(dev_ms, world)
+    clocks = clk.summary()
+    moe.synchronize(stream, ws)
+
+    ms_per_step = dev_ms / args.steps
+    tok_s = world * M * args.steps / (dev_ms / 1e3)
+
+    # --- e2e: host inputs -> public API -> host output, copies in the timed region
+    x_pin = torch.from_numpy(x_host.view(np.int16)).view(torch.bfloat16).pin_memory()
+    lg_pin = torch.from_numpy(lg_host).pin_memory()
+    y_pin = torch.empty(M, H, dtype=torch.bfloat16).pin_memory()
+    for _ in range(2):
+        with torch.cuda.stream(stream):
+            h.copy_(x_pin, non_blocking=True)
+            logits.copy_(lg_pin, non_blocking=True)
+            graph.replay()
+            y_pin.copy_(h, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            h.copy_(x_pin, non_blocking=True)
+            logits.copy_(lg_pin, non_blocking=True)
+            graph.replay()
+            y_pin.copy_(h, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_tok_s = world * M * args.steps / (e2e_ms / 1e3)
+    h2d = x_pin.numel() * 2 + lg_pin.numel() * 4
+    d2h = y_pin.numel() * 2
+
+    # --- live per-kernel durations (instrumented graph: one event pair per launch)
+    moe.profile_reset()
+    moe.profile_enable(True)
+    g2 = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g2, stream=stream):
+        step()
+    moe.profile_enable(False)
+    reps = max(3, min(args.steps, 10))
+    kt = {kid: [0.0, 0] for kid in range(4)}
+    try:
+        for _ in range(reps):
+            with torch.cuda.stream(stream):
+                g2.replay()
+            torch.cuda.synchronize()
+            for kid in range(4):
+                ms, n = moe.profile_read(kid)
+                kt[kid][0] += ms
+                kt[kid][1] += n
+    except moe.SeedlessError as e:
+        print(f"warning: per-kernel timing unavailable: {e}", file=sys.stderr)
+    moe.profile_reset()
+    del g2
+    avg = {kid: (kt[kid][0] / kt[kid][1] if kt[kid][1] else None) for kid in kt}
+    up_launch_bytes = (sum(uniq) / L) * up_bytes
+    peak, peak_kind = load_peaks()
+    achieved = up_launch_bytes / (avg[1] * 1e-3) / 1e9 if avg[1] else None
+    traffic = None
+    tf = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tf):
+        try:
+            traffic = json.load(open(tf)).get(args.config, {}).get("up_bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        wh, xh, ih, sh = host_layer_inputs(cfg, 0)
+        cpu = cpu_layer_sample(cfg, wh, xh, ih, sh, args.cpu_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u8xs8->s32 tensor-core dot, f32 epilogue, bf16 I/O",
+            "data": "synthetic (seeded generator, momij_b200/synth.py)",
+            "config": {"workload": cfg["desc"], "H": H, "E": E, "top_k": K, "I": I, "gs": gs,
+                       "M": M, "layers": L, "global_batch": M * world,
+                       "parallelism": "replicas" if world > 1 else "single",
+                       "l2": f"inputs larger than L2: {bytes_per_step / 1e9:.2f} GB of distinct "
+                             "expert weights streamed per step"},
+            "hbm_tbs": bytes_per_step / (ms_per_step * 1e-3) / 1e12,
+            "hbm_frac_of_peak": bytes_per_step / (ms_per_step * 1e-3) / 1e9 / peak,
+            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<up||gate+SwiGLU>",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": (achieved / peak) if achieved else None, "traffic": traffic,
+                         "peak_source": peak_kind,
+                         "bytes_per_launch": up_launch_bytes,
+                         "avg_launch_us": {"plan": _us(avg[0]), "up": _us(avg[1]),
+                                           "down": _us(avg[2]), "combine": _us(avg[3])}},
+            "clocks": clocks,
+            "e2e": {"value": e2e_tok_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / args.steps},
+            "gpu_launches": 4 * L * args.steps,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def _us(ms):
+    return None if ms is None else ms * 1e3
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="momij", choices=["momij", "reference"])
+    ap.add_argument("--config", default="decode", choices=sorted(CONFIGS))
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "momij" else args.warmup
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_gpu(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,189 @@
+/*
+ * momij_moe.h -- C ABI of libmomij_moe.so, a B200 (sm_100a) implementation of
+ * momij's 2-bit group-quantized MoE expert path.
+ *
+ * Every pointer argument is a device pointer owned by the caller (weights are
+ * aliased, never copied), every size is a plain int, and every entry point
+ * only enqueues work on `stream` (a cudaStream_t passed as void*; NULL is the
+ * legacy default stream) and returns a status code.  This is the encode-only
+ * convention of the reference's `into encoder:` overloads; the reference's
+ * nil-encoder overloads (commit + wait) correspond to calling the entry point
+ * and then momij_moe_synchronize().
+ *
+ * Weight format (MLX affine, transpose=true; momij WeightStore.swift:50-90):
+ *   w   uint32 [E, N, Kdim/16]  code k of a row at bits [2(k%16), 2(k%16)+1]
+ *   s,b dtype  [E, N, Kdim/gs]   dequantised weight = s*q + b, q in {0..3}
+ *   up||gate projection: N = 2I, rows [0,I) up, rows [I,2I) gate.
+ * Activations, scales, biases and outputs share one 16-bit dtype
+ * (MOMIJ_DTYPE_BF16 or MOMIJ_DTYPE_F16); router logits and scores are fp32;
+ * expert indices int32.  Accumulation is fp32 (exact integer dot products of
+ * the codes, fp32 scale/bias epilogue); every gather-GEMV output is rounded
+ * once to the activation dtype, as MLX gather_qmm outputs are.
+ *
+ * Supported shapes: gs in {64, 128}; Kdim % 256 == 0 and 256 <= Kdim <= 4096;
+ * any N >= 1; M*Ktop <= MOMIJ_MAX_PAIRS; for shared-x calls M <= 8.
+ */
+#ifndef MOMIJ_MOE_H
+#define MOMIJ_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* momij_stream_t; /* cudaStream_t */
+
+/* Status codes; the first three mirror SeedlessError
+ * (SeedlessMetal.swift:3718-3728). */
+enum momij_status {
+    MOMIJ_OK = 0,
+    MOMIJ_ERR_UNSUPPORTED_SHAPE = 1, /* SeedlessError.unsupportedShape(N,K,gs) */
+    MOMIJ_ERR_NOT_READY = 2,         /* SeedlessError.notReady */
+    MOMIJ_ERR_NO_DEVICE = 3,         /* SeedlessError.noMetal */
+    MOMIJ_ERR_INVALID_ARGUMENT = 4,  /* NULL pointer / negative size */
+    MOMIJ_ERR_EXPERT_INDEX = 5,      /* an expert index outside [0, E) (device-detected) */
+    MOMIJ_ERR_WORKSPACE = 6,         /* workspace too small */
+    MOMIJ_ERR_CUDA = 7,              /* a CUDA runtime call failed */
+    MOMIJ_ERR_NCCL = 8,              /* an NCCL call failed (expert parallel) */
+    MOMIJ_ERR_TIMEOUT = 9,           /* a bounded device-side wait gave up */
+    MOMIJ_ERR_STOPPED = 10           /* the stop flag was set */
+};
+
+enum momij_dtype { MOMIJ_DTYPE_BF16 = 0, MOMIJ_DTYPE_F16 = 1 };
+
+#define MOMIJ_MAX_PAIRS 1024
+
+/* Human-readable name of a status code (never NULL). */
+const char* momij_status_string(int status);
+
+/* Library/ABI version, e.g. 100 for 0.1.0. */
+int momij_version(void);
+
+/* Number of streaming multiprocessors of the current device, or -1. */
+int momij_device_sm_count(void);
+
+/* Waits for `stream`, then folds any device-detected error recorded in
+ * `workspace` (may be NULL) into the returned status. */
+int momij_moe_synchronize(momij_stream_t stream, const void* workspace);
+
+/* Router: fp32 softmax over logits [M,E]; top-K by K rounds of argmax on the
+ * logits (strict '>', so the lower index wins a tie); scores are the selected
+ * gates renormalised by their sum.  inds [M,K] int32 in descending-score
+ * order, scores [M,K] fp32.  K <= 32, E <= 1024.
+ * Replaces: maple_route_top8 + SeedlessMetal.encodeRoute
+ * (SeedlessMetal.swift:2720-2791, 1266-1281); MapleMoE.route
+ * (MapleMoE.swift:41-56). */
+int momij_moe_route(const float* logits, int M, int E, int K, int32_t* inds, float* scores,
+                    momij_stream_t stream);
+
+/* Per-expert token lists (counting sort by expert, ties by pair index):
+ * offsets [E+1], pair [M*K] (pair index m*K+k), weight [M*K] (its score).
+ * Replaces: nothing in the reference (MLX gather_qmm is called with
+ * sortedIndices:false, MapleMoE.swift:68); it is the permute step the
+ * grouped prefill GEMM and the expert-parallel dispatch consume. */
+int momij_moe_permute(const int32_t* inds, const float* scores, int M, int K, int E,
+                      int32_t* offsets, int32_t* pair, float* weight, momij_stream_t stream);
+
+/* Workspace bytes needed by momij_moe_gqmm2 / up_swiglu / expert_ffn /
+ * forward for these sizes (plan + staged intermediates).  The workspace must
+ * be zero-filled once before its first use; the kernels leave it reusable. */
+size_t momij_moe_workspace_size(int M, int Ktop, int H, int I);
+
+/* 2-bit gather-GEMV:
+ *   out[mk, n] = sum_k (s[e,n,k/gs]*q[e,n,k] + b[e,n,k/gs]) * x[row, k]
+ * with e = inds[mk], mk in [0, M*Ktop), row = mk if lhs_per_expert else
+ * mk / Ktop.  x [M or M*Ktop, Kdim], out [M*Ktop, N].  Each distinct expert's
+ * rows are streamed once per call (tokens sharing an expert share the load).
+ * Replaces: SeedlessMetal.gqmm2 (SeedlessMetal.swift:312-438, kernel
+ * gqmm2_rows :2168-2221) and MLX.gatherQuantizedMM(transpose:true, bits:2,
+ * mode:.affine) (MapleMoE.swift:65-75). */
+int momij_moe_gqmm2(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                    const int32_t* inds, void* out, int M, int Ktop, int Kdim, int N, int E, int gs,
+                    int lhs_per_expert, int dtype, void* workspace, size_t workspace_bytes,
+                    momij_stream_t stream);
+
+/* Fused up||gate gather-GEMV + clamped SwiGLU:
+ *   act[mk, j] = silu(min(g, clamp)) * clip(u, -clamp, clamp)
+ * with u, g the up row j and gate row I+j outputs (each rounded to dtype
+ * first).  x [M, H], w [E, 2I, H/16], act [M*Ktop, I].
+ * Replaces: SeedlessMetal.gqmm2UpSwiglu (SeedlessMetal.swift:441-484, kernel
+ * gqmm2_up_swiglu :2360-2433) and MapleMoE.clampedSwiglu over the split
+ * gather output (MapleMoE.swift:35-39, 65-70). */
+int momij_moe_gqmm2_up_swiglu(const void* x, const uint32_t* w, const void* scales,
+                              const void* biases, const int32_t* inds, void* act, int M, int Ktop,
+                              int H, int I, int E, int gs, float clamp, int dtype, void* workspace,
+                              size_t workspace_bytes, momij_stream_t stream);
+
+/* Elementwise clamped SwiGLU on ug [rows, 2I] (up || gate) -> act [rows, I].
+ * Replaces: maple_clamped_swiglu / encodeClampedSwiglu
+ * (SeedlessMetal.swift:2435-2450, 486-498). */
+int momij_moe_clamped_swiglu(const void* ug, void* act, int rows, int I, float clamp, int dtype,
+                             momij_stream_t stream);
+
+/* y[m, h] = cast(sum_k float(down[m*Ktop+k, h]) * scores[m*Ktop+k]).
+ * Replaces: maple_score_reduce / encodeScoreReduce (SeedlessMetal.swift:
+ * 2452-2470, 652-667) and the combine of MapleMoE.swift:76-78. */
+int momij_moe_score_reduce(const void* down, const float* scores, void* y, int M, int Ktop,
+                           int H, int dtype, momij_stream_t stream);
+
+/* h[m, h] = cast(float(h) + float(cast(acc))) with acc as in score_reduce.
+ * Replaces: maple_score_resid / encodeScoreResid (SeedlessMetal.swift:
+ * 2474-2493, 669-684). */
+int momij_moe_score_resid(const void* down, const float* scores, void* h, int M, int Ktop,
+                          int H, int dtype, momij_stream_t stream);
+
+/* Whole expert FFN for given routing: up||gate gather + SwiGLU, down gather,
+ * score-weighted combine.  If resid_h != NULL it is updated in place
+ * (h += y, two-kernel rounding) and y may be NULL.
+ * Replaces: SeedlessMetal.encodeFusedExpert / fusedExpertStep
+ * (SeedlessMetal.swift:503-572) and SeedlessMoELayer.run
+ * (MapleSeedlessMoE.swift:61-77). */
+int momij_moe_expert_ffn(const void* x, const uint32_t* w_ug, const void* s_ug, const void* b_ug,
+                         const uint32_t* w_dn, const void* s_dn, const void* b_dn,
+                         const int32_t* inds, const float* scores, void* y, void* resid_h, int M,
+                         int H, int I, int E, int Ktop, int gs, float clamp, int dtype,
+                         void* workspace, size_t workspace_bytes, momij_stream_t stream);
+
+/* Router + expert FFN from logits [M,E]: writes inds/scores (may be NULL to
+ * keep them in the workspace only) and y (or updates resid_h).
+ * Replaces: MapleMoE.callAsFunction (MapleMoE.swift:59-80) and the
+ * route + fused-expert part of SeedlessMetal.encodeMoEBlock
+ * (SeedlessMetal.swift:576-609). */
+int momij_moe_forward(const float* logits, const void* x, const uint32_t* w_ug, const void* s_ug,
+                      const void* b_ug, const uint32_t* w_dn, const void* s_dn, const void* b_dn,
+                      int32_t* inds, float* scores, void* y, void* resid_h, int M, int H, int I,
+                      int E, int Ktop, int gs, float clamp, int dtype, void* workspace,
+                      size_t workspace_bytes, momij_stream_t stream);
+
+/* Per-kernel GPU timing.  While enabled, each launch made by the entry points
+ * above is bracketed by two CUDA events on its stream (also when the stream
+ * is being captured into a CUDA graph; the pair then times the latest replay).
+ * momij_profile_read sums the recorded pairs of one kernel id (it waits for
+ * their events); momij_profile_reset releases all pairs.
+ * Replaces: the MOMIJ_PROFILE_MOE phase timers (MapleSeedlessMoE.swift:81-107)
+ * and the Metal GPU timestamps of the MoE benches (SeedlessMetal.swift:
+ * 1050-1069). */
+enum momij_kernel_id {
+    MOMIJ_KERNEL_PLAN = 0,    /* router and/or work plan */
+    MOMIJ_KERNEL_UP = 1,      /* up||gate gather-GEMV + SwiGLU */
+    MOMIJ_KERNEL_ROWS = 2,    /* gather-GEMV (down projection, gqmm2) */
+    MOMIJ_KERNEL_COMBINE = 3  /* score-weighted combine */
+};
+int momij_profile_enable(int on);
+int momij_profile_read(int kernel_id, double* total_ms, int* launches);
+int momij_profile_reset(void);
+
+/* Deterministic synthetic inputs (the generator of momij_b200/synth.py, bit
+ * for bit): kind 0 = packed 2-bit codes (uint32 words), 1 = a*u + c with u
+ * uniform in [0,1) rounded to dtype, 2 = Irwin-Hall normal rounded to dtype,
+ * 3 = Irwin-Hall normal as fp32.  Element i of dst gets index start + i.
+ * Test-input generation only; no counterpart in the reference. */
+int momij_synth_fill(void* dst, int64_t n, int kind, float a, float c, uint64_t seed,
+                     uint64_t stream_id, int64_t start, int dtype, momij_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOMIJ_MOE_H */

@@ -1,0 +1,96 @@
+// common.cuh -- device helpers shared by the momij MoE kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "momij_moe.h"
+
+namespace momij {
+
+constexpr int kWarp = 32;
+constexpr int kChunk = 256;          // codes of one row a warp handles per tile (64 B)
+constexpr int kDigitGroup = 64;      // x elements sharing one digit exponent
+constexpr int kDgStride = 200;       // bytes per digit group: three 64-B int8 planes + 8 B pad (bank spread)
+constexpr int kMaxTmax = 8;          // max pairs (token columns) per unit
+constexpr int kPlanHeader = 4;       // [0]=units, [1]=status, [2..3] reserved
+
+// ---- 16-bit float formats --------------------------------------------------
+template <int DT>
+struct Half;
+template <>
+struct Half<MOMIJ_DTYPE_BF16> {
+    static __device__ __forceinline__ float to_f(uint16_t h) {
+        return __uint_as_float(static_cast<uint32_t>(h) << 16);
+    }
+    static __device__ __forceinline__ uint16_t from_f(float f) {
+        // round to nearest even; NaN kept quiet
+        uint32_t u = __float_as_uint(f);
+        if ((u & 0x7fffffffu) > 0x7f800000u) return static_cast<uint16_t>((u >> 16) | 0x40u);
+        u += 0x7fffu + ((u >> 16) & 1u);
+        return static_cast<uint16_t>(u >> 16);
+    }
+};
+template <>
+struct Half<MOMIJ_DTYPE_F16> {
+    static __device__ __forceinline__ float to_f(uint16_t h) {
+        float f;
+        asm("{ cvt.f32.f16 %0, %1; }" : "=f"(f) : "h"(h));
+        return f;
+    }
+    static __device__ __forceinline__ uint16_t from_f(float f) {
+        uint16_t h;
+        asm("{ cvt.rn.f16.f32 %0, %1; }" : "=h"(h) : "f"(f));
+        return h;
+    }
+};
+
+// ---- tensor core: D(16x8 s32) += A(16x32 u8, row) * B(32x8 s8, col) --------
+// Fragment ownership (lane = 4*g + t): a0 (row g, k 4t..4t+3), a1 (row g+8,
+// same k), a2 (row g, k 16+4t..), a3 (row g+8, k 16+4t..); b0 (k 4t.., col g),
+// b1 (k 16+4t.., col g); d0,d1 (row g, cols 2t, 2t+1), d2,d3 (row g+8, ...).
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---- asynchronous global->shared copies ------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+    int n = valid ? 16 : 0;  // n == 0 zero-fills the destination, reads nothing
+    asm volatile("cp.async.cg.shared.global.L2::128B [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src),
+                 "r"(n));
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src, bool valid) {
+    int n = valid ? 8 : 0;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(dst), "l"(src), "r"(n));
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, bool valid) {
+    int n = valid ? 4 : 0;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst), "l"(src), "r"(n));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// ---- programmatic dependent launch -----------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;\n" ::);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+}  // namespace momij

@@ -1,0 +1,52 @@
+// kernels.cuh -- kernel declarations and launch-argument structs.
+#pragma once
+
+#include "common.cuh"
+
+namespace momij {
+
+// Gather-GEMV modes.
+enum GemvMode { kModeRows = 0, kModeUpSwiglu = 1 };
+
+struct GemvArgs {
+    const uint16_t* x;   // activation vectors, 16-bit, row length Kd
+    int x_per_pair;      // 1: vector of pair mk is x[mk]; 0: x[mk / Ktop]
+    int digit_all_tokens;  // 1: digitise all M token vectors once (shared x, M <= 8)
+    const uint32_t* w;   // [E, N, Kd/16]
+    const uint16_t* s;   // [E, N, Kd/gs]
+    const uint16_t* b;
+    int32_t* plan;       // see build_plan_block; plan[2] is the kernels' error word
+    uint16_t* out;       // [P, out_cols]
+    int Kd, N, E, M, Ktop, P;
+    int rows_per_unit;   // N (rows mode) or N/2 (up||gate row pairs)
+    int out_cols;
+    float clamp;
+    int nK, ptile;       // warps = nK * ptile
+    int max_units, max_tiles, max_vec, batch_rounds;
+    // dynamic shared-memory carve-up (byte offsets)
+    int off_tiles, off_units, off_upair, off_uslot, off_vecs, off_fs, off_dig, off_red, off_stage;
+};
+
+constexpr int kStageBytes = 1280;  // per warp per stage: 2 x 512 B codes + 256 B scales/biases
+
+__device__ void route_token_warp(const float* lg, int E, int K, int32_t* inds, float* scores);
+__global__ void route_kernel(const float* logits, int M, int E, int K, int32_t* inds,
+                             float* scores);
+__global__ void plan_kernel(const int32_t* inds, int P, int E, int tmax, int32_t* plan);
+__global__ void route_plan_kernel(const float* logits, int M, int E, int K, int tmax,
+                                  int32_t* inds, float* scores, int32_t* plan);
+__global__ void permute_kernel(const int32_t* inds, const float* scores, int P, int E,
+                               int32_t* offsets, int32_t* pair, float* weight, int32_t* status);
+
+template <int DT, int GS, int MODE, int TMAX, int STAGES>
+__global__ void gemv_kernel(const GemvArgs a);
+
+template <int DT>
+__global__ void swiglu_kernel(const uint16_t* ug, uint16_t* act, int rows, int I, float clamp);
+template <int DT, int RESID>
+__global__ void combine_kernel(const uint16_t* down, const float* scores, uint16_t* y, int M,
+                               int Ktop, int H, const int32_t* plan);
+__global__ void synth_fill_kernel(void* dst, int64_t n, int kind, float a, float c, uint64_t seed,
+                                  uint64_t stream_id, int64_t start, int dtype);
+
+}  // namespace momij

@@ -1,0 +1,244 @@
+// route.cu -- router top-k, per-expert token lists and the GEMV work plan.
+//
+// Router semantics follow maple_route_top8 (momij SeedlessMetal.swift:
+// 2720-2791): softmax in fp32, K rounds of argmax on the logits where a
+// strictly larger value replaces the running best (so the lower expert index
+// keeps a tie), scores are the selected gates divided by their sum.
+#include "kernels.cuh"
+
+namespace momij {
+
+// One warp routes one token: E <= 1024 (32 logits per lane), K <= 32.
+__device__ void route_token_warp(const float* __restrict__ lg, int E, int K,
+                                 int32_t* __restrict__ inds, float* __restrict__ scores) {
+    const int lane = threadIdx.x & 31;
+    float v[32];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        int e = lane + 32 * i;
+        v[i] = (e < E) ? lg[e] : -INFINITY;
+        mx = fmaxf(mx, v[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float z = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        if (lane + 32 * i < E) z += expf(v[i] - mx);
+    z = warp_sum(z);
+
+    uint32_t used = 0;
+    int my_ind = 0;
+    float my_gate = 0.f, sel_sum = 0.f;
+    for (int k = 0; k < K; ++k) {
+        float best = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            int e = lane + 32 * i;
+            if (e < E && !((used >> i) & 1u) && (bi == 0x7fffffff || v[i] > best)) {
+                best = v[i];
+                bi = e;  // i ascends, so a tie keeps the lower index
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            bool take = oi != 0x7fffffff &&
+                        (bi == 0x7fffffff || ob > best || (ob == best && oi < bi));
+            if (take) { best = ob; bi = oi; }
+        }
+        if ((bi & 31) == lane) used |= 1u << (bi >> 5);
+        float gate = expf(best - mx) / z;
+        sel_sum += gate;
+        if (lane == k) { my_ind = bi; my_gate = gate; }
+    }
+    if (lane < K) {
+        inds[lane] = my_ind;
+        scores[lane] = my_gate / sel_sum;
+    }
+}
+
+__global__ void route_kernel(const float* __restrict__ logits, int M, int E, int K,
+                             int32_t* __restrict__ inds, float* __restrict__ scores) {
+    pdl_wait();
+    const int warps = blockDim.x >> 5;
+    for (int m = blockIdx.x * warps + (threadIdx.x >> 5); m < M; m += gridDim.x * warps)
+        route_token_warp(logits + (size_t)m * E, E, K, inds + (size_t)m * K, scores + (size_t)m * K);
+    pdl_launch_dependents();
+}
+
+// ---- work plan for the gather-GEMV kernels ------------------------------
+// Sorts the P = M*Ktop pairs by (expert, pair index) and cuts each expert's
+// run into units of at most `tmax` pairs.  plan layout (int32):
+//   [0] units U, [1] plan status, [2] error word of the consuming kernels
+//   (reset here), [3] reserved,
+//   [4 + 4u .. 4 + 4u + 3] unit u = (expert, first sorted position, count, 0),
+//   [4 + 4P + q] pair index at sorted position q.
+// Runs as one block of 1024 threads; P <= MOMIJ_MAX_PAIRS.
+__device__ void build_plan_block(const int32_t* __restrict__ inds, int P, int E, int tmax,
+                                 int32_t* __restrict__ plan) {
+    __shared__ int s_e[MOMIJ_MAX_PAIRS];
+    __shared__ int s_flag[MOMIJ_MAX_PAIRS];
+    __shared__ int s_warp[32];
+    __shared__ int s_bad;
+    const int tid = threadIdx.x, nt = blockDim.x;
+    if (tid == 0) s_bad = 0;
+    __syncthreads();
+    for (int i = tid; i < P; i += nt) {
+        int e = inds[i];
+        if (e < 0 || e >= E) s_bad = 1;
+        s_e[i] = e;
+    }
+    __syncthreads();
+    if (s_bad) {
+        if (tid == 0) { plan[0] = 0; plan[1] = MOMIJ_ERR_EXPERT_INDEX; plan[2] = 0; }
+        return;
+    }
+    int32_t* units = plan + kPlanHeader;
+    int32_t* sorted = plan + kPlanHeader + 4 * P;
+    // stable rank of pair i among all pairs ordered by expert
+    int my_pos = -1, my_less = 0, my_before = 0, my_cnt = 0, my_e = 0;
+    if (tid < P) {
+        my_e = s_e[tid];
+        for (int j = 0; j < P; ++j) {
+            int ej = s_e[j];
+            my_less += ej < my_e;
+            my_cnt += ej == my_e;
+            my_before += (ej == my_e) & (j < tid);
+        }
+        my_pos = my_less + my_before;
+        s_flag[my_pos] = (my_before % tmax) == 0;
+        sorted[my_pos] = tid;
+    }
+    __syncthreads();
+    // exclusive scan of the unit-start flags over sorted positions (one per thread)
+    int f = (tid < P) ? s_flag[tid] : 0;
+    int incl = f;
+    const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int t = (lane < (nt >> 5)) ? s_warp[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += y;
+        }
+        s_warp[lane] = t;  // inclusive prefix of warp totals
+    }
+    __syncthreads();
+    int excl = incl - f + (warp > 0 ? s_warp[warp - 1] : 0);
+    __syncthreads();
+    // publish uid per sorted position back through s_flag
+    if (tid < P) s_flag[tid] = f ? excl : -1;
+    __syncthreads();
+    if (tid < P && (my_before % tmax) == 0) {
+        int u = s_flag[my_pos];
+        int cnt = my_cnt - my_before;
+        units[4 * u + 0] = my_e;
+        units[4 * u + 1] = my_pos;
+        units[4 * u + 2] = cnt < tmax ? cnt : tmax;
+        units[4 * u + 3] = 0;
+    }
+    if (tid == nt - 1) {
+        plan[0] = s_warp[(nt >> 5) - 1];
+        plan[1] = MOMIJ_OK;
+        plan[2] = 0;
+    }
+}
+
+__global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ inds, int P,
+                                                    int E, int tmax, int32_t* __restrict__ plan) {
+    pdl_wait();
+    build_plan_block(inds, P, E, tmax, plan);
+    pdl_launch_dependents();
+}
+
+// Router for all M tokens followed by the plan, in one block (decode sizes).
+__global__ void __launch_bounds__(1024) route_plan_kernel(const float* __restrict__ logits, int M,
+                                                          int E, int K, int tmax,
+                                                          int32_t* __restrict__ inds,
+                                                          float* __restrict__ scores,
+                                                          int32_t* __restrict__ plan) {
+    pdl_wait();
+    const int warps = blockDim.x >> 5;
+    for (int m = threadIdx.x >> 5; m < M; m += warps)
+        route_token_warp(logits + (size_t)m * E, E, K, inds + (size_t)m * K, scores + (size_t)m * K);
+    __syncthreads();
+    build_plan_block(inds, M * K, E, tmax, plan);
+    pdl_launch_dependents();
+}
+
+// ---- per-expert token lists (counting sort, stable in the pair index) ----
+// One block; warp w owns experts w, w+32, ...; each scans the P pairs in
+// order with ballots, so positions are deterministic.
+__global__ void __launch_bounds__(1024) permute_kernel(const int32_t* __restrict__ inds,
+                                                       const float* __restrict__ scores, int P,
+                                                       int E, int32_t* __restrict__ offsets,
+                                                       int32_t* __restrict__ pair,
+                                                       float* __restrict__ weight,
+                                                       int32_t* __restrict__ status) {
+    extern __shared__ int s_cnt[];  // E + 1
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    __shared__ int s_bad;
+    if (threadIdx.x == 0) s_bad = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        int e = inds[i];
+        if (e < 0 || e >= E) s_bad = 1;
+    }
+    __syncthreads();
+    if (s_bad) {
+        if (threadIdx.x == 0 && status) *status = MOMIJ_ERR_EXPERT_INDEX;
+        return;
+    }
+    for (int e = warp; e < E; e += nw) {
+        int c = 0;
+        for (int base = 0; base < P; base += 32) {
+            int i = base + lane;
+            c += __popc(__ballot_sync(0xffffffffu, i < P && inds[i] == e));
+        }
+        if (lane == 0) s_cnt[e] = c;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int carry = 0;
+        for (int base = 0; base < E; base += 32) {
+            int e = base + lane;
+            int v = e < E ? s_cnt[e] : 0, incl = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            if (e < E) offsets[e] = carry + incl - v;
+            carry += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) offsets[E] = carry;
+    }
+    __syncthreads();
+    for (int e = warp; e < E; e += nw) {
+        int pos = offsets[e];
+        for (int base = 0; base < P; base += 32) {
+            int i = base + lane;
+            bool hit = i < P && inds[i] == e;
+            uint32_t m = __ballot_sync(0xffffffffu, hit);
+            if (hit) {
+                int q = pos + __popc(m & ((1u << lane) - 1u));
+                pair[q] = i;
+                weight[q] = scores[i];
+            }
+            pos += __popc(m);
+        }
+    }
+}
+
+}  // namespace momij

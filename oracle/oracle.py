@@ -1,0 +1,226 @@
+"""Python access to the CPU oracle (TEST INFRASTRUCTURE ONLY).
+
+Two independent restatements of the reference's MoE expert semantics live
+here, so that each can check the other:
+
+* ``C`` -- ctypes bindings to ``lib/libmomij_oracle.so`` (moe_oracle.c), the
+  oracle the GPU parity tests and the CPU baseline use.
+* ``np_*`` -- a float64 numpy restatement written from the dense dequantised
+  weight matrix ``W = s*q + b`` (MLX affine, MapleMoE.swift:65-75 via
+  SeedlessMetal.swift:2145-2221), a different formulation from the C code's
+  per-group ``s*sum(q*x) + b*sum(x)`` factorisation.
+
+Parity against MLX gather_qmm itself is unpinned: MLX (mlx-swift 0.31.6) is
+not vendored and cannot run here.  Only tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline leg may use this module.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libmomij_oracle.so")
+
+_u16p = ctypes.POINTER(ctypes.c_uint16)
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+_f32p = ctypes.POINTER(ctypes.c_float)
+
+
+def build() -> str:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        c_int, c_float = ctypes.c_int, ctypes.c_float
+        L.oracle_route.argtypes = [_f32p, c_int, c_int, c_int, _i32p, _f32p]
+        L.oracle_permute.argtypes = [_i32p, _f32p, c_int, c_int, c_int, _i32p, _i32p, _f32p]
+        L.oracle_gqmm2.argtypes = [_u16p, _u32p, _u16p, _u16p, _i32p, _u16p] + [c_int] * 8
+        L.oracle_clamped_swiglu.argtypes = [_u16p, _u16p, c_int, c_int, c_float, c_int]
+        L.oracle_score_reduce.argtypes = [_u16p, _f32p, _u16p, c_int, c_int, c_int, c_int]
+        L.oracle_score_resid.argtypes = [_u16p, _f32p, _u16p, c_int, c_int, c_int, c_int]
+        L.oracle_expert_ffn.argtypes = ([_u16p, _u32p, _u16p, _u16p, _u32p, _u16p, _u16p, _i32p,
+                                         _f32p, _u16p, _u16p] + [c_int] * 6 + [c_float, c_int]
+                                        + [_u16p] * 3)
+        L.oracle_half_to_double.argtypes = [ctypes.c_uint16, c_int]
+        L.oracle_half_to_double.restype = ctypes.c_double
+        L.oracle_double_to_half.argtypes = [ctypes.c_double, c_int]
+        L.oracle_double_to_half.restype = ctypes.c_uint16
+        L.oracle_num_threads.restype = c_int
+        L.oracle_set_num_threads.argtypes = [c_int]
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray, t):
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(t)
+
+
+class OracleError(RuntimeError):
+    pass
+
+
+def route(logits: np.ndarray, K: int):
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    M, E = logits.shape
+    inds = np.zeros((M, K), np.int32)
+    scores = np.zeros((M, K), np.float32)
+    rc = lib().oracle_route(_p(logits, _f32p), M, E, K, _p(inds, _i32p), _p(scores, _f32p))
+    if rc:
+        raise OracleError(f"oracle_route rc={rc}")
+    return inds, scores
+
+
+def permute(inds: np.ndarray, scores: np.ndarray, E: int):
+    inds = np.ascontiguousarray(inds, np.int32)
+    scores = np.ascontiguousarray(scores, np.float32)
+    M, K = inds.shape
+    off = np.zeros(E + 1, np.int32)
+    pair = np.zeros(M * K, np.int32)
+    wt = np.zeros(M * K, np.float32)
+    rc = lib().oracle_permute(_p(inds, _i32p), _p(scores, _f32p), M, K, E, _p(off, _i32p),
+                              _p(pair, _i32p), _p(wt, _f32p))
+    if rc:
+        raise OracleError(f"oracle_permute rc={rc}")
+    return off, pair, wt
+
+
+def gqmm2(x, w, s, b, inds, M, Ktop, Kdim, N, gs, lhs_per_expert=False, dtype=0):
+    E = w.shape[0]
+    out = np.zeros((M * Ktop, N), np.uint16)
+    rc = lib().oracle_gqmm2(_p(x, _u16p), _p(w, _u32p), _p(s, _u16p), _p(b, _u16p),
+                            _p(np.ascontiguousarray(inds, np.int32), _i32p), _p(out, _u16p),
+                            M, Ktop, Kdim, N, E, gs, int(lhs_per_expert), dtype)
+    if rc:
+        raise OracleError(f"oracle_gqmm2 rc={rc}")
+    return out
+
+
+def clamped_swiglu(ug: np.ndarray, I: int, clamp: float = 7.0, dtype: int = 0):
+    rows = ug.shape[0]
+    act = np.zeros((rows, I), np.uint16)
+    lib().oracle_clamped_swiglu(_p(ug, _u16p), _p(act, _u16p), rows, I, clamp, dtype)
+    return act
+
+
+def score_reduce(down, scores, M, Ktop, H, dtype=0):
+    y = np.zeros((M, H), np.uint16)
+    lib().oracle_score_reduce(_p(down, _u16p), _p(np.ascontiguousarray(scores, np.float32), _f32p),
+                              _p(y, _u16p), M, Ktop, H, dtype)
+    return y
+
+
+def expert_ffn(x, wts: dict, inds, scores, M, H, I, Ktop, gs, clamp=7.0, dtype=0,
+               resid_h: np.ndarray | None = None):
+    """Returns (y, staged) where staged holds the rounded intermediates."""
+    E = wts["w_ug"].shape[0]
+    y = np.zeros((M, H), np.uint16)
+    ug = np.zeros((M * Ktop, 2 * I), np.uint16)
+    act = np.zeros((M * Ktop, I), np.uint16)
+    down = np.zeros((M * Ktop, H), np.uint16)
+    h = None if resid_h is None else np.ascontiguousarray(resid_h.copy())
+    rc = lib().oracle_expert_ffn(
+        _p(x, _u16p), _p(wts["w_ug"], _u32p), _p(wts["s_ug"], _u16p), _p(wts["b_ug"], _u16p),
+        _p(wts["w_dn"], _u32p), _p(wts["s_dn"], _u16p), _p(wts["b_dn"], _u16p),
+        _p(np.ascontiguousarray(inds, np.int32), _i32p),
+        _p(np.ascontiguousarray(scores, np.float32), _f32p), _p(y, _u16p),
+        None if h is None else _p(h, _u16p), M, H, I, E, Ktop, gs, clamp, dtype,
+        _p(ug, _u16p), _p(act, _u16p), _p(down, _u16p))
+    if rc:
+        raise OracleError(f"oracle_expert_ffn rc={rc}")
+    return (h if h is not None else y), {"ug": ug, "act": act, "down": down}
+
+
+def num_threads() -> int:
+    return int(lib().oracle_num_threads())
+
+
+def set_num_threads(n: int) -> None:
+    lib().oracle_set_num_threads(int(n))
+
+
+# ---- independent float64 numpy restatement --------------------------------
+
+def np_half_to_f64(h: np.ndarray, dtype: int = 0) -> np.ndarray:
+    h = np.asarray(h, np.uint16)
+    if dtype == 1:
+        return h.view(np.float16).astype(np.float64)
+    return (h.astype(np.uint32) << np.uint32(16)).view(np.float32).astype(np.float64)
+
+
+def np_f64_to_half(v: np.ndarray, dtype: int = 0) -> np.ndarray:
+    """Round float64 straight to bf16/fp16 (ties to even) via frexp/rint."""
+    v = np.asarray(v, np.float64)
+    mant = 10 if dtype == 1 else 7
+    expb = 5 if dtype == 1 else 8
+    bias = (1 << (expb - 1)) - 1
+    emin = 1 - bias
+    a = np.abs(v)
+    _, e = np.frexp(a)
+    e = np.maximum(e - 1, emin)
+    q = np.ldexp(1.0, e - mant)
+    r = np.rint(a / q) * q
+    with np.errstate(over="ignore"):
+        if dtype == 1:
+            out = r.astype(np.float16).view(np.uint16)
+        else:
+            out = (r.astype(np.float32).view(np.uint32) >> np.uint32(16)).astype(np.uint16)
+    out = np.where(np.signbit(v), out | np.uint16(0x8000), out).astype(np.uint16)
+    return out
+
+
+def np_dequant(w: np.ndarray, s: np.ndarray, b: np.ndarray, gs: int, dtype: int = 0) -> np.ndarray:
+    """[N, K/16] u32 + [N, K/gs] scales/biases -> dense float64 [N, K]."""
+    N, words = w.shape
+    shifts = (2 * np.arange(16, dtype=np.uint32))[None, None, :]
+    q = ((w[:, :, None] >> shifts) & np.uint32(3)).reshape(N, words * 16).astype(np.float64)
+    sf = np.repeat(np_half_to_f64(s, dtype), gs, axis=1)
+    bf = np.repeat(np_half_to_f64(b, dtype), gs, axis=1)
+    return sf * q + bf
+
+
+def np_route(logits: np.ndarray, K: int):
+    lg = np.asarray(logits, np.float64)
+    M, E = lg.shape
+    order = np.lexsort((np.broadcast_to(np.arange(E), lg.shape), -lg), axis=1)[:, :K]
+    p = np.exp(lg - lg.max(axis=1, keepdims=True))
+    p /= p.sum(axis=1, keepdims=True)
+    sel = np.take_along_axis(p, order, axis=1)
+    return order.astype(np.int32), (sel / sel.sum(axis=1, keepdims=True)).astype(np.float32)
+
+
+def np_gqmm2(x, w, s, b, inds, M, Ktop, gs, lhs_per_expert=False, dtype=0):
+    inds = np.asarray(inds).reshape(-1)
+    xf = np_half_to_f64(x, dtype)
+    outs = []
+    for mk in range(M * Ktop):
+        e = int(inds[mk])
+        W = np_dequant(w[e], s[e], b[e], gs, dtype)
+        xr = xf[mk if lhs_per_expert else mk // Ktop]
+        outs.append(W @ xr)
+    return np_f64_to_half(np.stack(outs), dtype)
+
+
+def np_expert_ffn(x, wts, inds, scores, M, H, I, Ktop, gs, clamp=7.0, dtype=0):
+    ug = np_gqmm2(x, wts["w_ug"], wts["s_ug"], wts["b_ug"], inds, M, Ktop, gs, False, dtype)
+    u = np.clip(np_half_to_f64(ug[:, :I], dtype), -clamp, clamp)
+    g = np.minimum(np_half_to_f64(ug[:, I:], dtype), clamp)
+    act = np_f64_to_half(g / (1.0 + np.exp(-g)) * u, dtype)
+    dn = np_gqmm2(act, wts["w_dn"], wts["s_dn"], wts["b_dn"], inds, M, Ktop, gs, True, dtype)
+    d = np_half_to_f64(dn, dtype).reshape(M, Ktop, H)
+    y = (d * np.asarray(scores, np.float64).reshape(M, Ktop, 1)).sum(axis=1)
+    return np_f64_to_half(y, dtype), {"ug": ug, "act": act, "down": dn}
