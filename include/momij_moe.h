@@ -104,6 +104,25 @@ int momij_moe_gqmm2(const void* x, const uint32_t* w, const void* scales, const 
                     int lhs_per_expert, int dtype, void* workspace, size_t workspace_bytes,
                     momij_stream_t stream);
 
+/* momij_moe_gqmm2 for callers that cannot allocate device memory (a binding
+ * that owns only its inputs and outputs, or an engine that forbids allocation
+ * inside its token loop because cudaMalloc can synchronize the device).  No
+ * counterpart in the reference.  Same arguments and results as
+ * momij_moe_gqmm2 minus the workspace: the work plan lives in a fixed
+ * 20,736-byte array compiled into the library (held on every GPU that loads
+ * it until exit), so the call allocates nothing.  Limits: M*Ktop <=
+ * MOMIJ_NOALLOC_MAX_PAIRS, otherwise MOMIJ_ERR_WORKSPACE; every call shares
+ * the array, so calls that overlap on the GPU race -- serialise them; the
+ * first call on a device looks up the array's address (cudaGetSymbolAddress)
+ * and should come before any stream capture on that device; an expert index
+ * out of range makes the call write nothing to `out`, and this entry point
+ * has no way to report it. */
+#define MOMIJ_NOALLOC_MAX_PAIRS 1024
+int momij_moe_gqmm2_noalloc(const void* x, const uint32_t* w, const void* scales,
+                            const void* biases, const int32_t* inds, void* out, int M, int Ktop,
+                            int Kdim, int N, int E, int gs, int lhs_per_expert, int dtype,
+                            momij_stream_t stream);
+
 /* Fused up||gate gather-GEMV + clamped SwiGLU:
  *   act[mk, j] = silu(min(g, clamp)) * clip(u, -clamp, clamp)
  * with u, g the up row j and gate row I+j outputs (each rounded to dtype
