@@ -188,11 +188,22 @@ enum momij_kernel_id {
     MOMIJ_KERNEL_PLAN = 0,    /* router and/or work plan */
     MOMIJ_KERNEL_UP = 1,      /* up||gate gather-GEMV + SwiGLU */
     MOMIJ_KERNEL_ROWS = 2,    /* gather-GEMV (down projection, gqmm2) */
-    MOMIJ_KERNEL_COMBINE = 3  /* score-weighted combine */
+    MOMIJ_KERNEL_COMBINE = 3, /* score-weighted combine */
+    MOMIJ_KERNEL_LAYER = 4    /* fused decode layer: route + up + down + combine */
 };
 int momij_profile_enable(int on);
 int momij_profile_read(int kernel_id, double* total_ms, int* launches);
 int momij_profile_reset(void);
+
+/* Phase trace of the fused decode-layer kernel: while a device buffer is set,
+ * each launch (also when captured into a graph) takes the next slot of
+ * (SM count x 16) int64 %globaltimer stamps, one row per CTA, written by the
+ * CTA's thread 0 at its phase boundaries (start, after the previous kernel,
+ * routed, planned, up tables, tokens encoded, up done, down prefetch issued,
+ * grid barrier passed, act encoded, down done, counters added, combined).
+ * NULL disables.  Counterpart: the reference's per-phase timers
+ * (PhaseMs, SeedlessDecodeEngine.swift:69-77). */
+int momij_layer_trace(void* device_buffer, size_t bytes);
 
 /* Deterministic synthetic inputs (the generator of momij_b200/synth.py, bit
  * for bit): kind 0 = packed 2-bit codes (uint32 words), 1 = a*u + c with u

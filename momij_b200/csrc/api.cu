@@ -12,6 +12,8 @@
 #include <vector>
 
 #include "kernels.cuh"
+#include "gemv_core.cuh"
+#include "layer.cuh"
 
 using namespace momij;
 
@@ -39,6 +41,10 @@ int current_device_sm_count() {
     return cache[dev];
 }
 
+// Dynamic shared memory a kernel of this library may request: the device's
+// per-block opt-in limit less a reserve for the kernels' static shared
+// memory (about 2 KB; the attribute call fails if the sum exceeds it).
+constexpr int kStaticSmemReserve = 4096;
 int max_dyn_smem() {
     static int cache[64] = {0};
     int dev = 0;
@@ -46,7 +52,7 @@ int max_dyn_smem() {
     if (cache[dev] == 0) {
         int n = 0;
         cudaDeviceGetAttribute(&n, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-        cache[dev] = n;
+        cache[dev] = n > kStaticSmemReserve ? n - kStaticSmemReserve : 0;
     }
     return cache[dev];
 }
@@ -133,6 +139,7 @@ struct Workspace {
     uint16_t* down;
     int32_t* inds;
     float* scores;
+    unsigned* block_ctr;
     size_t bytes;
 };
 
@@ -153,8 +160,195 @@ Workspace carve(void* ws, int M, int Ktop, int H, int I) {
     off += align_up(P * 4, 256);
     w.scores = reinterpret_cast<float*>(p + off);
     off += align_up(P * 4, 256);
+    w.block_ctr = reinterpret_cast<unsigned*>(p + off);
+    off += align_up((size_t)((H + 63) / 64) * 4, 256);
     w.bytes = off;
     return w;
+}
+
+// ---- fused MoE layer (layer.cu) -------------------------------------------
+constexpr int kNotApplicable = -1;
+
+LayerArgs layer_args(const float* logits, const int32_t* inds_in, const float* scores_in,
+                     int32_t* inds_out, float* scores_out, const void* x, const uint32_t* w_ug,
+                     const void* s_ug, const void* b_ug, const uint32_t* w_dn, const void* s_dn,
+                     const void* b_dn, void* y, void* resid_h, int M, int H, int I, int E, int K,
+                     float clamp) {
+    LayerArgs a{};
+    a.logits = logits;
+    a.inds_in = inds_in;
+    a.scores_in = scores_in;
+    a.inds_out = inds_out;
+    a.scores_out = scores_out;
+    a.x = static_cast<const uint16_t*>(x);
+    a.w_ug = w_ug;
+    a.s_ug = static_cast<const uint16_t*>(s_ug);
+    a.b_ug = static_cast<const uint16_t*>(b_ug);
+    a.w_dn = w_dn;
+    a.s_dn = static_cast<const uint16_t*>(s_dn);
+    a.b_dn = static_cast<const uint16_t*>(b_dn);
+    a.y = resid_h ? nullptr : static_cast<uint16_t*>(y);
+    a.h = static_cast<uint16_t*>(resid_h);
+    a.M = M;
+    a.H = H;
+    a.I = I;
+    a.E = E;
+    a.K = K;
+    a.clamp = clamp;
+    return a;
+}
+
+using LayerFn = void (*)(const LayerArgs);
+
+template <int DT, int GS>
+LayerFn pick_layer_tm(int tmax) {
+    switch (tmax) {
+        case 1: return moe_layer_kernel<DT, GS, 1, kLayerStages>;
+        case 2: return moe_layer_kernel<DT, GS, 2, kLayerStages>;
+        case 4: return moe_layer_kernel<DT, GS, 4, kLayerStages>;
+        default: return moe_layer_kernel<DT, GS, 8, kLayerStages>;
+    }
+}
+LayerFn pick_layer(int dtype, int gs, int tmax) {
+    if (dtype == MOMIJ_DTYPE_BF16)
+        return gs == 64 ? pick_layer_tm<MOMIJ_DTYPE_BF16, 64>(tmax)
+                        : pick_layer_tm<MOMIJ_DTYPE_BF16, 128>(tmax);
+    return gs == 64 ? pick_layer_tm<MOMIJ_DTYPE_F16, 64>(tmax)
+                    : pick_layer_tm<MOMIJ_DTYPE_F16, 128>(tmax);
+}
+
+// Phase tracing of fused-layer launches (momij_layer_trace).
+std::mutex g_trace_mu;
+long long* g_trace_buf = nullptr;
+size_t g_trace_slots = 0, g_trace_next = 0;
+
+long long* next_trace_slot(int G) {
+    std::lock_guard<std::mutex> lk(g_trace_mu);
+    if (!g_trace_buf || g_trace_slots == 0) return nullptr;
+    long long* p = g_trace_buf + (g_trace_next % g_trace_slots) * (size_t)G * kTracePoints;
+    ++g_trace_next;
+    return p;
+}
+
+bool fused_enabled() {
+    const char* v = std::getenv("MOMIJ_FUSED");
+    return !(v && v[0] == '0');
+}
+
+// Launches the whole layer as one cooperative kernel when the batch is a
+// decode/verify batch that fits; kNotApplicable lets the caller fall back to
+// the multi-kernel path (same arithmetic, same bits).
+int run_fused_layer(LayerArgs a, int dtype, int gs, const Workspace& ws, cudaStream_t st) {
+    const int P = a.M * a.K;
+    if (!fused_enabled() || a.M > 8 || P > kLayerMaxPairs || a.E > 1024 || a.K > 32)
+        return kNotApplicable;
+    const int tmax = pick_tmax(a.M);
+    const int stages = kLayerStages;
+    const int rt = item_tiles(tmax);
+    const int G = current_device_sm_count();
+    if (G <= 0) return kNotApplicable;
+    a.nK_up = a.H / kChunk;
+    a.nK_dn = a.I / kChunk;
+    // rank top-k when its comparisons stay within ~256 per thread
+    a.route_parts = 0;
+    if ((long long)a.M * a.E * a.E <= (long long)kLayerThreads * 256) {
+        int parts = 1;
+        while (parts < 32 && (long long)a.M * a.E * parts * 2 <= kLayerThreads && a.E % (parts * 2) == 0)
+            parts *= 2;
+        a.route_parts = parts;
+    }
+    const long long rows_up = ((long long)P * a.I + G - 1) / G;
+    const long long rows_dn = ((long long)P * a.H + G - 1) / G;
+    const int mu_up = (int)std::min<long long>(P, rows_up / a.I + 2);
+    const int mu_dn = (int)std::min<long long>(P, rows_dn / a.H + 2);
+    const int mt_up = (int)(rows_up / 8 + mu_up + 1);
+    const int mt_dn = (int)(rows_dn / 16 + mu_dn + 1);
+    if (rows_dn / 64 + 2 * mu_dn > kLayerMaxLastBlocks) return kNotApplicable;
+    const int max_units = std::max(mu_up, mu_dn), max_tiles = std::max(mt_up, mt_dn);
+    const int vec_dn = std::min(P, mu_dn * tmax);
+    a.max_tiles = max_tiles;
+    a.max_units = max_units;
+    a.max_vec = vec_dn;
+    const size_t ndg = std::max((size_t)a.M * (a.H / 64), (size_t)vec_dn * (a.I / 64));
+    const size_t limit = (size_t)max_dyn_smem();
+    {
+        size_t off = 0;
+        a.off_logits = (int)off; off += a.logits ? 4 * (size_t)a.M * a.E : 0;
+        a.off_inds = (int)off; off += 4 * (size_t)P;
+        a.off_scores = (int)off; off += 4 * (size_t)P;
+        a.off_sorted = (int)off; off += 4 * (size_t)P;
+        off = align_up(off, 16);
+        a.off_pflag = (int)off; off += 16 * (size_t)P;  // per sorted pair: (expert, before, count)
+        a.off_units = (int)off; off += 16 * (size_t)P;
+        a.off_tiles_up = (int)off; off += 16 * (size_t)max_tiles;
+        a.off_lunits_up = (int)off; off += 16 * (size_t)max_units;
+        a.off_seg_up = (int)off; off += 16 * (size_t)max_units;
+        a.off_tiles_dn = (int)off; off += 16 * (size_t)max_tiles;
+        a.off_lunits_dn = (int)off; off += 16 * (size_t)max_units;
+        a.off_seg_dn = (int)off; off += 16 * (size_t)max_units;
+        a.off_upair_up = (int)off; off += 4 * (size_t)max_units * tmax;
+        a.off_uslot_up = (int)off; off += 4 * (size_t)max_units * tmax;
+        a.off_upair_dn = (int)off; off += 4 * (size_t)max_units * tmax;
+        a.off_uslot_dn = (int)off; off += 4 * (size_t)max_units * tmax;
+        a.off_xvecs = (int)off; off += 4 * (size_t)a.M;
+        a.off_vecs_dn = (int)off; off += 4 * (size_t)vec_dn;
+        off = align_up(off, 16);
+        a.off_fs = (int)off; off += 8 * ndg;
+        off = align_up(off, 16);
+        a.off_dig = (int)off; off += (size_t)kDgStride * ndg;
+        off = align_up(off, 16);
+        a.off_red = (int)off;
+        // the red buffer takes what the ring leaves, up to all tiles at once
+        const size_t ring = (size_t)kConsumerWarps * stages * slot_bytes(tmax);
+        if (off + ring + 128 > limit) return kNotApplicable;
+        const size_t red_bytes = limit - off - ring - 128;
+        const size_t pt_up = 4 * (size_t)a.nK_up * tmax * 16, pt_dn = 4 * (size_t)a.nK_dn * tmax * 16;
+        const size_t all_up = (size_t)(mt_up + rt - 1) / rt * rt, all_dn = (size_t)(mt_dn + rt - 1) / rt * rt;
+        a.batch_up = (int)std::min(all_up, red_bytes / pt_up / rt * rt);
+        a.batch_dn = (int)std::min(all_dn, red_bytes / pt_dn / rt * rt);
+        if (a.batch_up < rt || a.batch_dn < rt) return kNotApplicable;
+        off += std::max(a.batch_up * pt_up, a.batch_dn * pt_dn);
+        off = align_up(off, 128);
+        a.off_stage = (int)off; off += ring;
+        LayerFn fn = pick_layer(dtype, gs, tmax);
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)off) !=
+            cudaSuccess)
+            return MOMIJ_ERR_CUDA;
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kLayerThreads, off) !=
+                cudaSuccess ||
+            per_sm < 1)
+            return kNotApplicable;
+        a.trace = next_trace_slot(G);
+        a.ctrl = ws.plan;
+        a.ctrl_u = reinterpret_cast<unsigned*>(ws.plan);
+        a.block_ctr = ws.block_ctr;
+        a.act = ws.act;
+        a.down = ws.down;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(G);
+        cfg.blockDim = dim3(kLayerThreads);
+        cfg.dynamicSmemBytes = off;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        static bool pdl_with_coop = true;  // dropped if the driver refuses the pair
+        cfg.numAttrs = (pdl_enabled() && pdl_with_coop) ? 2 : 1;
+        const int slot = prof_begin(MOMIJ_KERNEL_LAYER, st);
+        cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a);
+        if (e != cudaSuccess && cfg.numAttrs == 2) {
+            cudaGetLastError();
+            pdl_with_coop = false;
+            cfg.numAttrs = 1;
+            e = cudaLaunchKernelEx(&cfg, fn, a);
+        }
+        prof_end(slot, st);
+        return cuda_status(e);
+    }
 }
 
 // ---- gather-GEMV dispatch --------------------------------------------------
@@ -162,12 +356,12 @@ using GemvFn = void (*)(const GemvArgs);
 
 template <int DT, int GS, int MODE>
 GemvFn pick_tm_st(int tmax, int stages) {
-    const bool s8 = stages == 8;
+    const bool s4 = stages == 4;
     switch (tmax) {
-        case 1: return s8 ? gemv_kernel<DT, GS, MODE, 1, 8> : gemv_kernel<DT, GS, MODE, 1, 4>;
-        case 2: return s8 ? gemv_kernel<DT, GS, MODE, 2, 8> : gemv_kernel<DT, GS, MODE, 2, 4>;
-        case 4: return s8 ? gemv_kernel<DT, GS, MODE, 4, 8> : gemv_kernel<DT, GS, MODE, 4, 4>;
-        default: return s8 ? gemv_kernel<DT, GS, MODE, 8, 8> : gemv_kernel<DT, GS, MODE, 8, 4>;
+        case 1: return s4 ? gemv_kernel<DT, GS, MODE, 1, 4> : gemv_kernel<DT, GS, MODE, 1, 2>;
+        case 2: return s4 ? gemv_kernel<DT, GS, MODE, 2, 4> : gemv_kernel<DT, GS, MODE, 2, 2>;
+        case 4: return s4 ? gemv_kernel<DT, GS, MODE, 4, 4> : gemv_kernel<DT, GS, MODE, 4, 2>;
+        default: return s4 ? gemv_kernel<DT, GS, MODE, 8, 4> : gemv_kernel<DT, GS, MODE, 8, 2>;
     }
 }
 template <int DT, int GS>
@@ -191,15 +385,12 @@ struct GemvLaunch {
 
 // Worst-case shared-memory sizing from (P, shapes); returns false if the
 // configuration cannot fit on the device.
-bool configure_gemv(GemvLaunch& L, int mode, int tmax) {
+bool configure_gemv(GemvLaunch& L, int mode, int tmax, int gs) {
+    (void)gs;
     GemvArgs& a = L.a;
     const int nK = a.Kd / kChunk;
-    int ptile = nK >= 16 ? 1 : 16 / nK;
-    if (ptile > 4) ptile = 4;
     a.nK = nK;
-    a.ptile = ptile;
-    const int warps = nK * ptile;
-    L.threads = 32 * warps;
+    L.threads = kGemvThreads;
     const int TR = mode == kModeUpSwiglu ? 8 : 16;
     const long long Ru = a.rows_per_unit;
     const long long Rmax = (long long)a.P * Ru;
@@ -214,39 +405,42 @@ bool configure_gemv(GemvLaunch& L, int mode, int tmax) {
     a.max_tiles = (int)(rows_cta / TR + a.max_units + 1);
     a.max_vec = a.digit_all_tokens ? a.M : std::min(a.P, a.max_units * tmax);
     const int nDG = a.Kd / kDigitGroup;
-    const int nrounds = (a.max_tiles + ptile - 1) / ptile;
 
     const size_t limit = (size_t)max_dyn_smem();
-    for (int stages : {8, 4}) {
-        for (int rounds = std::min(nrounds, 32); rounds >= 1; rounds = rounds > 1 ? rounds / 2 : 0) {
-            size_t off = 0;
-            a.off_tiles = (int)off; off += 16 * (size_t)a.max_tiles;
-            a.off_units = (int)off; off += 16 * (size_t)a.max_units;
-            a.off_upair = (int)off; off += 4 * (size_t)a.max_units * tmax;
-            a.off_uslot = (int)off; off += 4 * (size_t)a.max_units * tmax;
-            a.off_vecs = (int)off; off += 4 * (size_t)a.max_vec;
-            off = align_up(off, 16);
-            a.off_fs = (int)off; off += 8 * (size_t)a.max_vec * nDG;
-            off = align_up(off, 16);
-            a.off_dig = (int)off; off += (size_t)kDgStride * a.max_vec * nDG;
-            off = align_up(off, 16);
-            a.off_red = (int)off; off += 4 * (size_t)rounds * ptile * nK * tmax * 16;
-            off = align_up(off, 128);
-            a.off_stage = (int)off; off += (size_t)warps * stages * kStageBytes;
-            if (off <= limit) {
-                a.batch_rounds = rounds;
-                L.stages = stages;
-                L.smem = off;
-                return true;
-            }
-            if (rounds == 1) break;
-        }
+    const int rt = item_tiles(tmax);
+    const size_t pt = 4 * (size_t)nK * tmax * 16;  // red_floats_per_tile
+    for (int stages : {4, 2}) {
+        size_t off = 0;
+        a.off_tiles = (int)off; off += 16 * (size_t)a.max_tiles;
+        a.off_units = (int)off; off += 16 * (size_t)a.max_units;
+        a.off_upair = (int)off; off += 4 * (size_t)a.max_units * tmax;
+        a.off_uslot = (int)off; off += 4 * (size_t)a.max_units * tmax;
+        a.off_vecs = (int)off; off += 4 * (size_t)a.max_vec;
+        off = align_up(off, 16);
+        a.off_fs = (int)off; off += 8 * (size_t)a.max_vec * nDG;
+        off = align_up(off, 16);
+        a.off_dig = (int)off; off += (size_t)kDgStride * a.max_vec * nDG;
+        off = align_up(off, 16);
+        a.off_red = (int)off;
+        // the red buffer takes what the ring leaves, up to all tiles at once
+        const size_t ring = (size_t)kConsumerWarps * stages * slot_bytes(tmax);
+        if (off + ring + 128 > limit) continue;
+        const size_t bt = std::min((size_t)(a.max_tiles + rt - 1) / rt * rt,
+                                   (limit - off - ring - 128) / pt / rt * rt);
+        if (bt < (size_t)rt) continue;
+        a.batch_tiles = (int)bt;
+        off += bt * pt;
+        off = align_up(off, 128);
+        a.off_stage = (int)off; off += ring;
+        L.stages = stages;
+        L.smem = off;
+        return true;
     }
     return false;
 }
 
 int run_gemv(GemvLaunch& L, int mode, int tmax, int dtype, int gs, cudaStream_t st) {
-    if (!configure_gemv(L, mode, tmax)) return MOMIJ_ERR_UNSUPPORTED_SHAPE;
+    if (!configure_gemv(L, mode, tmax, gs)) return MOMIJ_ERR_UNSUPPORTED_SHAPE;
     GemvFn fn = pick_gemv(dtype, gs, mode, tmax, L.stages);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.smem);
     if (e != cudaSuccess) return MOMIJ_ERR_CUDA;
@@ -401,6 +595,20 @@ int momij_profile_read(int kernel_id, double* total_ms, int* launches) {
     return MOMIJ_OK;
 }
 
+int momij_layer_trace(void* device_buffer, size_t bytes) {
+    std::lock_guard<std::mutex> lk(g_trace_mu);
+    const int G = current_device_sm_count();
+    if (!device_buffer || bytes == 0 || G <= 0) {
+        g_trace_buf = nullptr;
+        g_trace_slots = 0;
+        return device_buffer ? MOMIJ_ERR_INVALID_ARGUMENT : MOMIJ_OK;
+    }
+    g_trace_buf = static_cast<long long*>(device_buffer);
+    g_trace_slots = bytes / ((size_t)G * kTracePoints * sizeof(long long));
+    g_trace_next = 0;
+    return g_trace_slots ? MOMIJ_OK : MOMIJ_ERR_WORKSPACE;
+}
+
 int momij_profile_reset(void) {
     std::lock_guard<std::mutex> lk(g_prof_mu);
     for (auto& r : g_prof) r.used = false;
@@ -416,6 +624,11 @@ int momij_moe_synchronize(momij_stream_t stream, const void* workspace) {
     if (cudaMemcpy(hdr, workspace, sizeof(hdr), cudaMemcpyDeviceToHost) != cudaSuccess)
         return MOMIJ_ERR_CUDA;
     if (hdr[1] != MOMIJ_OK) return hdr[1];
+    if (hdr[2] != MOMIJ_OK) {
+        // the error word is sticky on the device; report it once
+        int32_t* err = static_cast<int32_t*>(const_cast<void*>(workspace)) + 2;
+        if (cudaMemset(err, 0, sizeof(int32_t)) != cudaSuccess) return MOMIJ_ERR_CUDA;
+    }
     return hdr[2];
 }
 
@@ -575,6 +788,10 @@ int momij_moe_expert_ffn(const void* x, const uint32_t* w_ug, const void* s_ug, 
     if (M == 0) return MOMIJ_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     Workspace ws = carve(workspace, M, Ktop, H, I);
+    LayerArgs la = layer_args(nullptr, inds, scores, nullptr, nullptr, x, w_ug, s_ug, b_ug, w_dn,
+                              s_dn, b_dn, y, resid_h, M, H, I, E, Ktop, clamp);
+    const int frc = run_fused_layer(la, dtype, gs, ws, st);
+    if (frc != kNotApplicable) return frc;
     const int tmax = tmax_for(M, Ktop, 0);
     int rc = launch_plan(inds, M * Ktop, E, tmax, ws.plan, st);
     if (rc) return rc;
@@ -599,6 +816,10 @@ int momij_moe_forward(const float* logits, const void* x, const uint32_t* w_ug, 
     Workspace ws = carve(workspace, M, Ktop, H, I);
     int32_t* ind_out = inds ? inds : ws.inds;
     float* sc_out = scores ? scores : ws.scores;
+    LayerArgs la = layer_args(logits, nullptr, nullptr, ind_out, sc_out, x, w_ug, s_ug, b_ug, w_dn,
+                              s_dn, b_dn, y, resid_h, M, H, I, E, Ktop, clamp);
+    const int frc = run_fused_layer(la, dtype, gs, ws, st);
+    if (frc != kNotApplicable) return frc;
     const int tmax = tmax_for(M, Ktop, 0);
     const int slot = prof_begin(MOMIJ_KERNEL_PLAN, st);
     int rc = cuda_status(launch(route_plan_kernel, dim3(1), dim3(1024), 0, st, logits, M, E, Ktop,

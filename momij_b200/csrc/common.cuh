@@ -45,6 +45,19 @@ struct Half<MOMIJ_DTYPE_F16> {
     }
 };
 
+// Clamped SwiGLU with the reference's rounding staging: the up and gate
+// gather outputs are activation-dtype values first (MLX gather_qmm outputs,
+// MapleMoE.swift:65-70), the SwiGLU runs in fp32 on them and is rounded once
+// (maple_clamped_swiglu, SeedlessMetal.swift:2435-2450).
+template <int DT>
+__device__ __forceinline__ uint16_t swiglu_staged(float up, float gate, float clamp) {
+    float u = Half<DT>::to_f(Half<DT>::from_f(up));
+    float g = Half<DT>::to_f(Half<DT>::from_f(gate));
+    g = fminf(g, clamp);
+    u = fminf(fmaxf(u, -clamp), clamp);
+    return Half<DT>::from_f(g / (1.f + expf(-g)) * u);
+}
+
 // ---- tensor core: D(16x8 s32) += A(16x32 u8, row) * B(32x8 s8, col) --------
 // Fragment ownership (lane = 4*g + t): a0 (row g, k 4t..4t+3), a1 (row g+8,
 // same k), a2 (row g, k 16+4t..), a3 (row g+8, k 16+4t..); b0 (k 4t.., col g),
@@ -67,6 +80,19 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool v
     asm volatile("cp.async.cg.shared.global.L2::128B [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src),
                  "r"(n));
 }
+// The same copies with an L2 eviction-priority policy (createpolicy).
+__device__ __forceinline__ void cp_async16_hint(uint32_t dst, const void* src, bool valid,
+                                                uint64_t policy) {
+    int n = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;\n" ::"r"(dst),
+                 "l"(src), "r"(n), "l"(policy));
+}
+__device__ __forceinline__ void cp_async8_hint(uint32_t dst, const void* src, bool valid,
+                                               uint64_t policy) {
+    int n = valid ? 8 : 0;
+    asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 8, %2, %3;\n" ::"r"(dst),
+                 "l"(src), "r"(n), "l"(policy));
+}
 __device__ __forceinline__ void cp_async8(uint32_t dst, const void* src, bool valid) {
     int n = valid ? 8 : 0;
     asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(dst), "l"(src), "r"(n));
@@ -79,6 +105,57 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// ---- mbarriers and TMA bulk copies (no multicast) ---------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+// Arrives on `bar` once every cp.async this thread issued so far has landed
+// (the barrier's expected count includes this arrival).
+__device__ __forceinline__ void mbar_arrive_cp_async(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+    return p;
+}
+// Global -> shared bulk copy completing on `bar` (16-B aligned, 16-B multiple).
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;\n" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+// Named barrier over `count` threads (a subset of the block).
+__device__ __forceinline__ void bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
 
 // ---- programmatic dependent launch -----------------------------------------

@@ -21,15 +21,13 @@ struct GemvArgs {
     int rows_per_unit;   // N (rows mode) or N/2 (up||gate row pairs)
     int out_cols;
     float clamp;
-    int nK, ptile;       // warps = nK * ptile
-    int max_units, max_tiles, max_vec, batch_rounds;
+    int nK;              // 256-code chunks per row
+    int max_units, max_tiles, max_vec;
+    int batch_tiles;     // tiles per epilogue batch (a multiple of item_tiles)
     // dynamic shared-memory carve-up (byte offsets)
     int off_tiles, off_units, off_upair, off_uslot, off_vecs, off_fs, off_dig, off_red, off_stage;
 };
 
-constexpr int kStageBytes = 1280;  // per warp per stage: 2 x 512 B codes + 256 B scales/biases
-
-__device__ void route_token_warp(const float* lg, int E, int K, int32_t* inds, float* scores);
 __global__ void route_kernel(const float* logits, int M, int E, int K, int32_t* inds,
                              float* scores);
 __global__ void plan_kernel(const int32_t* inds, int P, int E, int tmax, int32_t* plan);

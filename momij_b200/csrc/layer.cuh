@@ -1,0 +1,56 @@
+// layer.cuh -- arguments of the fused MoE layer kernel (layer.cu).
+#pragma once
+
+#include "kernels.cuh"
+
+namespace momij {
+
+// Control words at the start of the workspace (shared with the work-plan
+// header of the multi-kernel path): [1] status of the call's routing,
+// [2] sticky error word (bounded waits that gave up), [3] grid-barrier
+// counter.  Per-64-row completion counters live in their own region.
+constexpr int kCtrlStatus = 1, kCtrlError = 2, kCtrlBarrier = 3;
+constexpr int kLayerMaxLastBlocks = 64;
+constexpr int kLayerThreads = 512;  // 16 warps that load and compute
+constexpr int kLayerMaxPairs = 64;
+constexpr int kLayerStages = 4;  // ring slots per warp (items in flight + 1)
+constexpr int kTracePoints = 16;  // phase stamps per CTA when tracing (momij_layer_trace)
+
+struct LayerArgs {
+    const float* logits;     // [M, E] or nullptr (then inds_in/scores_in)
+    const int32_t* inds_in;  // [M, K]
+    const float* scores_in;
+    int32_t* inds_out;       // optional copies of the routing (CTA 0 writes)
+    float* scores_out;
+    const uint16_t* x;       // [M, H]
+    const uint32_t* w_ug;
+    const uint16_t* s_ug;
+    const uint16_t* b_ug;
+    const uint32_t* w_dn;
+    const uint16_t* s_dn;
+    const uint16_t* b_dn;
+    uint16_t* act;           // [M*K, I] staged SwiGLU output
+    uint16_t* down;          // [M*K, H] staged down-projection output
+    uint16_t* y;             // [M, H] output, or nullptr when h is set
+    uint16_t* h;             // residual stream updated in place (may alias x)
+    int32_t* ctrl;           // control words (see above)
+    unsigned* ctrl_u;        // same words, unsigned view
+    unsigned* block_ctr;     // [ceil(H/64)] completion counters, zero between calls
+    int M, H, I, E, K;
+    int route_parts;  // threads per candidate of the rank top-k (a power of two dividing E), 0: per-warp rounds
+    float clamp;
+    int nK_up, nK_dn;        // 256-code chunks per row of each phase
+    int batch_up, batch_dn;  // tiles per epilogue batch of each phase (multiples of item_tiles)
+    int max_tiles, max_units, max_vec;  // capacities of the shared-memory tables
+    long long* trace;  // optional: kTracePoints %globaltimer stamps per CTA (thread 0)
+    // dynamic shared-memory carve-up (byte offsets)
+    int off_logits, off_inds, off_scores, off_sorted, off_pflag, off_units;
+    int off_tiles_up, off_lunits_up, off_upair_up, off_uslot_up, off_seg_up, off_xvecs;
+    int off_tiles_dn, off_lunits_dn, off_upair_dn, off_uslot_dn, off_seg_dn, off_vecs_dn;
+    int off_fs, off_dig, off_red, off_stage;
+};
+
+template <int DT, int GS, int TMAX, int STAGES>
+__global__ void moe_layer_kernel(const LayerArgs a);
+
+}  // namespace momij

@@ -5,61 +5,9 @@
 // strictly larger value replaces the running best (so the lower expert index
 // keeps a tie), scores are the selected gates divided by their sum.
 #include "kernels.cuh"
+#include "route_core.cuh"
 
 namespace momij {
-
-// One warp routes one token: E <= 1024 (32 logits per lane), K <= 32.
-__device__ void route_token_warp(const float* __restrict__ lg, int E, int K,
-                                 int32_t* __restrict__ inds, float* __restrict__ scores) {
-    const int lane = threadIdx.x & 31;
-    float v[32];
-    float mx = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        int e = lane + 32 * i;
-        v[i] = (e < E) ? lg[e] : -INFINITY;
-        mx = fmaxf(mx, v[i]);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float z = 0.f;
-#pragma unroll
-    for (int i = 0; i < 32; ++i)
-        if (lane + 32 * i < E) z += expf(v[i] - mx);
-    z = warp_sum(z);
-
-    uint32_t used = 0;
-    int my_ind = 0;
-    float my_gate = 0.f, sel_sum = 0.f;
-    for (int k = 0; k < K; ++k) {
-        float best = -INFINITY;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            int e = lane + 32 * i;
-            if (e < E && !((used >> i) & 1u) && (bi == 0x7fffffff || v[i] > best)) {
-                best = v[i];
-                bi = e;  // i ascends, so a tie keeps the lower index
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            float ob = __shfl_xor_sync(0xffffffffu, best, o);
-            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            bool take = oi != 0x7fffffff &&
-                        (bi == 0x7fffffff || ob > best || (ob == best && oi < bi));
-            if (take) { best = ob; bi = oi; }
-        }
-        if ((bi & 31) == lane) used |= 1u << (bi >> 5);
-        float gate = expf(best - mx) / z;
-        sel_sum += gate;
-        if (lane == k) { my_ind = bi; my_gate = gate; }
-    }
-    if (lane < K) {
-        inds[lane] = my_ind;
-        scores[lane] = my_gate / sel_sum;
-    }
-}
 
 __global__ void route_kernel(const float* __restrict__ logits, int M, int E, int K,
                              int32_t* __restrict__ inds, float* __restrict__ scores) {

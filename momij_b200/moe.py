@@ -66,6 +66,7 @@ def _load() -> ctypes.CDLL:
     L.momij_synth_fill.argtypes = [vp, ctypes.c_int64, i, f, f, ctypes.c_uint64,
                                    ctypes.c_uint64, ctypes.c_int64, i, vp]
     L.momij_profile_enable.argtypes = [i]
+    L.momij_layer_trace.argtypes = [vp, sz]
     L.momij_profile_read.argtypes = [i, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i)]
     return L
 
@@ -222,7 +223,7 @@ def forward(logits, x, wts: dict, y=None, *, H: int, I: int, Ktop: int, gs: int 
 
 # ---- per-kernel timing ----------------------------------------------------------
 
-KERNEL_PLAN, KERNEL_UP, KERNEL_ROWS, KERNEL_COMBINE = 0, 1, 2, 3
+KERNEL_PLAN, KERNEL_UP, KERNEL_ROWS, KERNEL_COMBINE, KERNEL_LAYER = 0, 1, 2, 3, 4
 
 
 def profile_enable(on: bool = True) -> None:

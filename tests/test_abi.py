@@ -32,9 +32,10 @@ def test_workspace_size_grows_with_pairs():
     a = moe.workspace_size(1, 8, 4096, 1536)
     b = moe.workspace_size(8, 8, 4096, 1536)
     assert 0 < a < b
-    # plan (header + 5 ints per pair) + act + down + inds + scores, 256-B aligned pieces
+    # plan (header + 5 ints per pair) + act + down + inds + scores + one
+    # completion counter per 64 output rows, 256-B aligned pieces
     P = 8
-    expect = (-(-(4 * (4 + 5 * P)) // 256) * 256 + P * 1536 * 2 + P * 4096 * 2 + 256 + 256)
+    expect = (-(-(4 * (4 + 5 * P)) // 256) * 256 + P * 1536 * 2 + P * 4096 * 2 + 256 + 256 + 256)
     assert a == expect
     assert moe.workspace_size(-1, 8, 16, 16) == 0
 

@@ -229,6 +229,49 @@ def test_fused_expert_matches_oracle(M, H, I, E, K, gs, dt):
     assert_ffn_parity(h, h_ref, st["down"], scores, dt, "fused expert resid")
 
 
+@pytest.mark.parametrize("M,H,I,E,K,gs,dt,rho", [
+    (1, 1024, 512, 16, 4, 64, 0, None),
+    (8, 2048, 1024, 64, 8, 64, 0, 0.7),
+    (3, 768, 1536, 24, 6, 128, 1, 0.7),
+    (5, 4096, 256, 32, 8, 64, 0, None),
+])
+def test_fused_layer_matches_multikernel_path(M, H, I, E, K, gs, dt, rho, monkeypatch):
+    """The one-kernel decode layer (route + up + grid barrier + down +
+    last-arriver combine) and the multi-kernel path (route/plan, up, down,
+    combine kernels) run the same arithmetic: same bits, several calls in a
+    row on one workspace (the completion counters reset themselves)."""
+    w = S.expert_weights(E, H, I, gs, seed=13, dtype=dt)
+    dw = dev_weights(w, dt)
+    ws = moe.new_workspace(M, K, H, I)
+    outs = {}
+    for path in ("1", "0"):
+        monkeypatch.setenv("MOMIJ_FUSED", path)
+        for call in range(3):
+            x = S.activations(M, H, layer=call, seed=13, dtype=dt)
+            lg = (S.logits_ar1(M, E, rho, call, 13) if rho else S.logits_normal(M, E, call, 13))
+            y = torch.empty(M, H, dtype=TD[dt], device=DEV)
+            h = dev16(S.normal_half(M * H, 13, 99, dt).reshape(M, H), dt)
+            inds = torch.empty(M, K, dtype=torch.int32, device=DEV)
+            scores = torch.empty(M, K, dtype=torch.float32, device=DEV)
+            moe.forward(torch.from_numpy(lg).to(DEV), dev16(x, dt), dw, y, H=H, I=I, Ktop=K, gs=gs,
+                        M=M, inds=inds, scores=scores, workspace=ws)
+            moe.forward(torch.from_numpy(lg).to(DEV), dev16(x, dt), dw, None, H=H, I=I, Ktop=K,
+                        gs=gs, M=M, resid_h=h, workspace=ws)
+            moe.synchronize(workspace=ws)
+            outs[(path, call)] = (host16(y), host16(h), inds.cpu().numpy(), scores.cpu().numpy())
+    for call in range(3):
+        f, m = outs[("1", call)], outs[("0", call)]
+        for a, b in zip(f, m):
+            assert (a == b).all(), call
+    # and against the oracle
+    x = S.activations(M, H, layer=0, seed=13, dtype=dt)
+    lg = (S.logits_ar1(M, E, rho, 0, 13) if rho else S.logits_normal(M, E, 0, 13))
+    i_ref, s_ref = O.route(lg, K)
+    y_ref, st = O.expert_ffn(x, w, i_ref, s_ref, M, H, I, K, gs, 7.0, dt)
+    assert (outs[("1", 0)][2] == i_ref).all()
+    assert_ffn_parity(outs[("1", 0)][0], y_ref, st["down"], s_ref, dt, "fused layer")
+
+
 def test_fused_expert_mrow_matches_sequential():
     """Batched M=4 equals four M=1 steps exactly (MomijCoreTests.swift:317-405)."""
     M, H, I, E, K, gs = 4, 1024, 512, 16, 4, 64
