@@ -297,17 +297,27 @@ int run_fused_layer(LayerArgs a, int dtype, int gs, const Workspace& ws, cudaStr
         off = align_up(off, 16);
         a.off_dig = (int)off; off += (size_t)kDgStride * ndg;
         off = align_up(off, 16);
-        a.off_red = (int)off;
-        // the red buffer takes what the ring leaves, up to all tiles at once
+        // the red and scale/bias buffers take what the ring leaves, up to a
+        // whole phase per batch; the phases share them
         const size_t ring = (size_t)kConsumerWarps * stages * slot_bytes(tmax);
-        if (off + ring + 128 > limit) return kNotApplicable;
-        const size_t red_bytes = limit - off - ring - 128;
-        const size_t pt_up = 4 * (size_t)a.nK_up * tmax * 16, pt_dn = 4 * (size_t)a.nK_dn * tmax * 16;
-        const size_t all_up = (size_t)(mt_up + rt - 1) / rt * rt, all_dn = (size_t)(mt_dn + rt - 1) / rt * rt;
-        a.batch_up = (int)std::min(all_up, red_bytes / pt_up / rt * rt);
-        a.batch_dn = (int)std::min(all_dn, red_bytes / pt_dn / rt * rt);
-        if (a.batch_up < rt || a.batch_dn < rt) return kNotApplicable;
-        off += std::max(a.batch_up * pt_up, a.batch_dn * pt_dn);
+        if (off + ring + 256 > limit) return kNotApplicable;
+        const size_t avail = limit - off - ring - 256;
+        const size_t rpt_up = 4 * (size_t)a.nK_up * tmax * 16, rpt_dn = 4 * (size_t)a.nK_dn * tmax * 16;
+        const size_t spt_up = sb_bytes_per_tile(a.H, gs), spt_dn = sb_bytes_per_tile(a.I, gs);
+        size_t bu = (size_t)(mt_up + rt - 1) / rt * rt, bd = (size_t)(mt_dn + rt - 1) / rt * rt;
+        auto need = [&]() {
+            return std::max(bu * rpt_up, bd * rpt_dn) + std::max(bu * spt_up, bd * spt_dn) + 16;
+        };
+        while (need() > avail && (bu > (size_t)rt || bd > (size_t)rt)) {
+            if (bu * (rpt_up + spt_up) >= bd * (rpt_dn + spt_dn) && bu > (size_t)rt) bu = std::max((size_t)rt, (bu / 2 + rt - 1) / rt * rt);
+            else bd = std::max((size_t)rt, (bd / 2 + rt - 1) / rt * rt);
+        }
+        if (need() > avail) return kNotApplicable;
+        a.batch_up = (int)bu;
+        a.batch_dn = (int)bd;
+        a.off_red = (int)off; off += std::max(bu * rpt_up, bd * rpt_dn);
+        off = align_up(off, 16);
+        a.off_sb = (int)off; off += std::max(bu * spt_up, bd * spt_dn);
         off = align_up(off, 128);
         a.off_stage = (int)off; off += ring;
         LayerFn fn = pick_layer(dtype, gs, tmax);
@@ -386,7 +396,6 @@ struct GemvLaunch {
 // Worst-case shared-memory sizing from (P, shapes); returns false if the
 // configuration cannot fit on the device.
 bool configure_gemv(GemvLaunch& L, int mode, int tmax, int gs) {
-    (void)gs;
     GemvArgs& a = L.a;
     const int nK = a.Kd / kChunk;
     a.nK = nK;
@@ -421,15 +430,20 @@ bool configure_gemv(GemvLaunch& L, int mode, int tmax, int gs) {
         off = align_up(off, 16);
         a.off_dig = (int)off; off += (size_t)kDgStride * a.max_vec * nDG;
         off = align_up(off, 16);
-        a.off_red = (int)off;
-        // the red buffer takes what the ring leaves, up to all tiles at once
+        // the red and scale/bias buffers take what the ring leaves, up to
+        // all tiles at once
         const size_t ring = (size_t)kConsumerWarps * stages * slot_bytes(tmax);
-        if (off + ring + 128 > limit) continue;
+        if (off + ring + 256 > limit) continue;
+        const size_t spt = sb_bytes_per_tile(a.Kd, gs);
         const size_t bt = std::min((size_t)(a.max_tiles + rt - 1) / rt * rt,
-                                   (limit - off - ring - 128) / pt / rt * rt);
+                                   (limit - off - ring - 256) / (pt + spt) / rt * rt);
         if (bt < (size_t)rt) continue;
         a.batch_tiles = (int)bt;
+        a.off_red = (int)off;
         off += bt * pt;
+        off = align_up(off, 16);
+        a.off_sb = (int)off;
+        off += bt * spt;
         off = align_up(off, 128);
         a.off_stage = (int)off; off += ring;
         L.stages = stages;

@@ -28,6 +28,7 @@ template <int DT, int GS, int MODE, int TMAX, int STAGES>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ int s_ntiles, s_nvec, s_overflow;
+    __shared__ __align__(8) uint64_t s_sbar;
     const int tid = threadIdx.x;
     constexpr int TR = GemvPhase<DT, GS, MODE, TMAX, STAGES>::TR;
 
@@ -100,15 +101,21 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
 
     PhaseTables tabs{s_tiles, s_units, s_uslot, s_ntiles};
     PhaseWeights wts{a.w, a.s, a.b, a.N, a.rows_per_unit, a.Kd};
-    GemvPhase<DT, GS, MODE, TMAX, STAGES> ph(tabs, wts, s_stage, 0, a.nK);
+    sb_init(&s_sbar);
+    GemvPhase<DT, GS, MODE, TMAX, STAGES> ph(tabs, wts, s_stage, 0, a.nK,
+                                             reinterpret_cast<uint16_t*>(smem + a.off_sb), a.batch_tiles,
+                                             &s_sbar);
     auto ahead = [&]() { ph.load_next(); };
+    bar_sync(kBarConsumers, kConsumerThreads);  // the scale/bias mbarrier is initialised
+    if (s_ntiles > 0) ph.issue_sb(0, min(s_ntiles, a.batch_tiles));
     ph.prefetch(ahead);
     // encode the activations while the first items land
     digitize<DT>(a.x, s_vecs, s_nvec, a.Kd, s_dig, s_fs, kConsumerThreads);
     bar_sync(kBarConsumers, kConsumerThreads);
     StoreOut<DT, MODE, TMAX> out{s_upair, a.out, a.out_cols, a.clamp};
-    ph.consume(s_dig, s_fs, s_red, a.batch_tiles, out, ahead);
+    const bool ok = ph.consume(s_dig, s_fs, s_red, true, out, ahead);
     ring_quiesce();
+    if (!ok && tid == 0) atomicExch(a.plan + 2, MOMIJ_ERR_TIMEOUT);
     pdl_launch_dependents();
 }
 

@@ -43,6 +43,7 @@ constexpr int kConsumerWarps = 16;
 constexpr int kConsumerThreads = 32 * kConsumerWarps;
 constexpr int kGemvThreads = kConsumerThreads;
 constexpr int kBarConsumers = 1;  // named barrier id used by the consumer warps
+constexpr int kWaitLimit = 1 << 22;  // bounded mbarrier waits (then MOMIJ_ERR_TIMEOUT)
 
 // Balanced base-256 digits of |v| < 2^22: v = 65536*d[0] + 256*d[1] + d[2],
 // d[1], d[2] in [-128, 127], d[0] in [-64, 64].
@@ -139,12 +140,16 @@ struct PhaseWeights {
     int Kd;
 };
 
-// Tiles per item: one-/two-token units take two tiles (32 MMA rows) per
-// item, which share the item's B fragments and bookkeeping; larger units one.
-__host__ __device__ constexpr int item_tiles(int tmax) { return tmax <= 2 ? 2 : 1; }
-// One warp's ring slot: the 16 * item_tiles MMA rows of one 256-code chunk
-// (64 B each), then their scales [rows][256/gs] and biases (halves).
-__host__ __device__ constexpr int slot_bytes(int tmax) { return item_tiles(tmax) * (16 * 64 + 2 * 16 * 4 * 2); }
+// An item is one tile (16 MMA rows) x two adjacent 256-code chunks, i.e. 128
+// code bytes -- one whole cache line -- per row: the copies of a warp then
+// request four full lines per instruction.
+__host__ __device__ constexpr int item_tiles(int) { return 1; }
+constexpr int kItemChunks = 2;
+// One warp's ring slot: the 16 rows x 128 code bytes of one item.
+__host__ __device__ constexpr int slot_bytes(int) { return 16 * 128; }
+// Scale/bias buffer of an epilogue batch: scales [tiles * 16][Kd/gs] then
+// biases (halves); MMA row r of the batch's tile k at row 16 k + r.
+__host__ __device__ constexpr int sb_bytes_per_tile(int Kd, int gs) { return 16 * (Kd / gs) * 2 * 2; }
 
 // Red-buffer floats per tile: [nK][TMAX][16 rows], each the sum of the four
 // lane groups' partials of one chunk, (t0 + t1) + (t2 + t3).
@@ -176,7 +181,8 @@ __device__ __forceinline__ float tile_sum(const float* red, int nK, int j, int r
 }
 
 // Epilogue of tiles [tfirst, tlast) whose partials are in red_base (tile
-// tau at (tau - tfirst) * per_tile), block-wide, 8 lanes per output:
+// tau at (tau - tfirst) * per_tile), block-wide, 8 lanes per output (they
+// read different chunks, so no bank conflicts between tiles):
 // out(tile, j, r, v, v_gate) for every valid output (v_gate: the gate row's
 // sum in up||gate mode).  Every thread of the block calls it.
 template <int TMAX, int MODE, class Out>
@@ -210,69 +216,77 @@ struct GemvPhase {
     static constexpr int TR = (MODE == kModeUpSwiglu) ? 8 : 16;  // output rows per tile
     static constexpr int DIST = STAGES - 1;  // items in flight ahead of the one computed
     static constexpr int SPC = 256 / GS;     // scale groups per row of a chunk
-    static constexpr int RT = item_tiles(TMAX);
-    static constexpr int ROWS = 16 * RT;     // MMA rows per item
-    static constexpr int CODE_BYTES = ROWS * 64;
     static constexpr int SLOT = slot_bytes(TMAX);
 
-    // Position in the warp's item sequence: tile group (RT tiles) and chunk.
+    // Position in the warp's item sequence: tile and chunk pair.
     struct Iter {
-        int grp, c, n;  // n: items of this phase passed so far
+        int tile, cp, n;  // n: items of this phase passed so far
     };
 
     PhaseTables T;
     PhaseWeights W;
     unsigned char* ring;  // this warp's STAGES slots
     int q0;               // ring position of this warp's first item of the phase
-    int warp, lane, g, t, nK, count, dgrp, dc;
-    bool sb8;  // scales/biases copied as 8-B pieces (else 4-B)
+    int warp, lane, g, t, nK, ncp, count, dtile, dcp;
     uint64_t policy;
     Iter li, ci;  // next item to load, next item to compute
     float* red;   // partials of the current batch of tiles
     int tfirst;   // first tile of the current batch
     int per_tile;
+    uint16_t* sb;   // the batch's scales, then biases (sb_bytes_per_tile per tile)
+    int sb_tiles;   // tiles the scale/bias buffer holds (the batch size)
+    uint64_t* sbar; // mbarrier of the batch's scale/bias copies
+    int sb_par;     // its phase parity
+    bool sb16;      // scale/bias rows and tensors 16-B aligned (16-B copies, else 4-B)
 
     // ring_base: the block's rings (kConsumerWarps x STAGES x SLOT);
-    // q0_: items this warp streamed through its ring in earlier phases.
+    // q0_: items this warp streamed through its ring in earlier phases;
+    // sb_, sb_tiles_: the scale/bias buffer (batch size in tiles); sbar_: an
+    // mbarrier initialised by sb_init.
     __device__ GemvPhase(const PhaseTables& tabs, const PhaseWeights& wts, unsigned char* ring_base,
-                         int q0_, int nK_)
-        : T(tabs), W(wts), q0(q0_), nK(nK_) {
+                         int q0_, int nK_, uint16_t* sb_, int sb_tiles_, uint64_t* sbar_)
+        : T(tabs), W(wts), q0(q0_), nK(nK_), sb(sb_), sb_tiles(sb_tiles_), sbar(sbar_), sb_par(0) {
+        const int nsb = W.Kd / GS;
+        sb16 = (nsb * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(W.s) % 16) == 0 &&
+               (reinterpret_cast<uintptr_t>(W.b) % 16) == 0 && (reinterpret_cast<uintptr_t>(sb) % 16) == 0;
         per_tile = red_floats_per_tile<TMAX>(nK_);
         warp = threadIdx.x >> 5;
         lane = threadIdx.x & 31;
         g = lane >> 2;
         t = lane & 3;
         ring = ring_base + (size_t)warp * STAGES * SLOT;
-        const int nitems = ((T.ntiles + RT - 1) / RT) * nK;
+        ncp = (nK + kItemChunks - 1) / kItemChunks;
+        const int nitems = T.ntiles * ncp;
         count = warp < nitems ? (nitems - warp + kConsumerWarps - 1) / kConsumerWarps : 0;
-        dgrp = kConsumerWarps / nK;
-        dc = kConsumerWarps - dgrp * nK;
-        li.grp = warp / nK;
-        li.c = warp - li.grp * nK;
+        dtile = kConsumerWarps / ncp;
+        dcp = kConsumerWarps - dtile * ncp;
+        li.tile = warp / ncp;
+        li.cp = warp - li.tile * ncp;
         li.n = 0;
         ci = li;
-        sb8 = SPC == 4 && (reinterpret_cast<uintptr_t>(W.s) % 8) == 0 &&
-              (reinterpret_cast<uintptr_t>(W.b) % 8) == 0;
         policy = l2_evict_first_policy();
     }
 
-    // Item k of this warp is (tile group, chunk) number warp + 16 k of the
-    // phase, group-major, so the 16 warps stream neighbouring chunks of the
+    // Item k of this warp is (tile, chunk pair) number warp + 16 k of the
+    // phase, tile-major, so the 16 warps stream neighbouring chunks of the
     // same rows at the same time.
     __device__ __forceinline__ void advance(Iter& it) const {
-        it.c += dc;
-        it.grp += dgrp;
-        if (it.c >= nK) {
-            it.c -= nK;
-            ++it.grp;
+        it.cp += dcp;
+        it.tile += dtile;
+        if (it.cp >= ncp) {
+            it.cp -= ncp;
+            ++it.tile;
         }
         ++it.n;
     }
 
-    // Offset of 32-byte half h of MMA row r's 64 code bytes in a slot: the
-    // halves of rows 2 and 3 (mod 4) are swapped, so the 8-byte reads of four
-    // consecutive rows by a half-warp fall into distinct banks.
-    static __device__ __forceinline__ int swz(int r, int h) { return 32 * (h ^ ((r >> 1) & 1)); }
+    // Slot offset of 16-byte granule j (0..7) of MMA row r's 128 code bytes:
+    // granules are permuted by j ^ f(r), f(r) = {0, 1, 4, 5}[r & 3], so the
+    // 8-byte reads of four consecutive rows by a half-warp (two granules 2
+    // apart per row) fall into distinct banks.
+    static __device__ __forceinline__ int swz(int r, int j) {
+        return r * 128 + 16 * (j ^ ((r & 1) | ((r & 2) << 1)));
+    }
 
     // Global row of MMA row r (0..15) of tile `tile`, or -1 beyond the tile.
     __device__ __forceinline__ int tile_row(const int4& tile, int r) const {
@@ -286,58 +300,75 @@ struct GemvPhase {
 
     // Copies the next item into its slot and commits one cp.async group (an
     // empty one past the end, so the group count stays in step with the
-    // items).  Rows beyond the tiles are zero-filled.
+    // items).  Rows beyond the tile, and the second chunk when nK is odd, are
+    // zero-filled.  Lane l copies granule l & 7 of rows (l >> 3) + 4 k.
     __device__ void load_next() {
         if (li.n < count) {
             const uint32_t dst = smem_u32(ring + ((q0 + li.n) % STAGES) * SLOT);
-            int4 tile[RT];
-            size_t eb[RT];
-#pragma unroll
-            for (int rt = 0; rt < RT; ++rt) {
-                const int tau = li.grp * RT + rt;
-                tile[rt] = (tau < T.ntiles) ? T.tiles[tau] : make_int4(0, 0, 0, 0);
-                eb[rt] = (size_t)T.units[tile[rt].x].x * W.N;
-            }
-            const int ra = lane >> 2, part = lane & 3;
+            const int4 tile = T.tiles[li.tile];
+            const int part = lane & 7, r0 = lane >> 3;
+            const bool pvalid = kItemChunks * li.cp + (part >> 2) < nK;
             const size_t rs = (size_t)(W.Kd >> 4);
-            const size_t co = (size_t)li.c * 16 + part * 4;
+            // rows r0 + 4k: up||gate: k = 0, 1 up rows, k = 2, 3 the gate rows
+            const uint32_t* p0 =
+                W.w + ((size_t)T.units[tile.x].x * W.N + tile.y + r0) * rs + (size_t)li.cp * 32 + part * 4;
+            const uint32_t* p2 = (MODE == kModeUpSwiglu) ? p0 + (size_t)W.Ru * rs : p0 + 8 * rs;
+            const int lim = (MODE == kModeUpSwiglu) ? tile.z : tile.z - 8;  // rows valid in p2's block
 #pragma unroll
-            for (int rt = 0; rt < RT; ++rt) {
-#pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    const int row = tile_row(tile[rt], ra + 8 * hh);
-                    const int mr = rt * 16 + ra + 8 * hh;
-                    cp_async16_hint(dst + mr * 64 + swz(mr, part >> 1) + 16 * (part & 1),
-                                    W.w + (row >= 0 ? (eb[rt] + row) * rs + co : 0), row >= 0,
-                                    policy);
-                }
-            }
-            // scales then biases of the item's rows: piece lane + 32 k ->
-            // (tensor, row); 2 * ROWS = 32 * RT pieces
-#pragma unroll
-            for (int k = 0; k < RT; ++k) {
-                const int it = lane + 32 * k;
-                const int sb = it / ROWS, r = it - sb * ROWS;
-                const bool second = RT > 1 && r >= 16;  // row of the item's second tile
-                const int4 tl = second ? tile[RT - 1] : tile[0];
-                const size_t ebr = second ? eb[RT - 1] : eb[0];
-                const int row = tile_row(tl, r & 15);
-                const uint16_t* src =
-                    (sb ? W.b : W.s) +
-                    (row >= 0 ? (ebr + row) * (size_t)(W.Kd / GS) + (size_t)li.c * SPC : 0);
-                const uint32_t sdst = dst + CODE_BYTES + (sb * ROWS + r) * SPC * 2;
-                if (sb8) {
-                    cp_async8_hint(sdst, src, row >= 0, policy);
-                } else {
-#pragma unroll
-                    for (int k = 0; k < SPC / 2; ++k) cp_async4(sdst + 4 * k, src + 2 * k, row >= 0);
-                }
+            for (int k = 0; k < 4; ++k) {
+                const int ri = r0 + 4 * (k & 1);
+                const bool v = pvalid && ri < ((k < 2) ? tile.z : lim);
+                const uint32_t* src = ((k < 2) ? p0 : p2) + (size_t)(4 * (k & 1)) * rs;
+                cp_async16_hint(dst + swz(r0 + 4 * k, part), v ? src : W.w, v, policy);
             }
             advance(li);
         } else {
             ++li.n;
         }
         cp_async_commit();
+    }
+
+    // Scales and biases of tiles [tb0, tb1) into sb; every thread calls it
+    // and then arrives on sbar (count kConsumerThreads) once its copies have
+    // landed.  16-B cp.async pieces walk each row contiguously (4-B pieces
+    // when rows or tensors are not 16-B aligned).
+    __device__ void issue_sb(int tb0, int tb1) {
+        constexpr int PARTS = (MODE == kModeUpSwiglu) ? 2 : 1;
+        constexpr int PR = 16 / PARTS;  // MMA rows per part of a tile
+        const int nsb = W.Kd / GS;
+        const int psz = sb16 ? 16 : 4;
+        const int ppr = nsb * 2 / psz;  // pieces per row
+        const int per_tile = 2 * 16 * ppr;
+        // this thread's pieces within a tile: i = threadIdx.x + 512 j
+        for (int i = threadIdx.x; i < per_tile; i += kConsumerThreads) {
+            const int tensor = i / (16 * ppr), rr = i - tensor * 16 * ppr;
+            const int r = rr / ppr, pc = rr - r * ppr;
+            const int part = r / PR, ri = r - part * PR;
+            const uint16_t* gsrc = tensor ? W.b : W.s;
+            const size_t goff = ((size_t)part * W.Ru + ri) * nsb;
+            const uint32_t dst0 =
+                smem_u32(sb + ((size_t)tensor * sb_tiles * 16 + r) * nsb) + pc * psz;
+            for (int k = tb0; k < tb1; ++k) {
+                const int4 tile = T.tiles[k];
+                if (ri >= tile.z) continue;
+                const size_t grow = (size_t)T.units[tile.x].x * W.N + tile.y;
+                const unsigned char* src =
+                    reinterpret_cast<const unsigned char*>(gsrc + grow * nsb + goff) + pc * psz;
+                const uint32_t dst = dst0 + (uint32_t)((k - tb0) * 16 * nsb * 2);
+                if (sb16) cp_async16(dst, src, true);
+                else cp_async4(dst, src, true);
+            }
+        }
+        mbar_arrive_cp_async(sbar);
+    }
+    // Before computing a batch: its scales and biases have landed (bounded
+    // wait; false if it gave up).
+    __device__ bool wait_sb() {
+        const uint32_t par = sb_par & 1;
+        ++sb_par;
+        for (int it = 0; it < kWaitLimit; ++it)
+            if (mbar_try_wait(sbar, par)) return true;
+        return false;
     }
 
     // Issues the first DIST items of the warp's item sequence through
@@ -349,61 +380,62 @@ struct GemvPhase {
         for (int j = 0; j < DIST; ++j) ahead();
     }
 
-    // MMA layout.  For K half h (code bytes 32h..32h+31 of the chunk, digit
-    // groups 2h and 2h+1) and code class p, lane (g, t) holds the A bytes
-    // 32h + 8t + [0, 8) of MMA rows g and g + 8 (MMA k = 4t + i <-> byte
-    // 8t + i, k = 16 + 4t + i <-> byte 8t + 4 + i), i.e. bytes of digit group
-    // 2h + (t >> 1).  B column n is (local group n >> 2, digit n & 3), digit 3
-    // unused: a lane's B registers are non-zero only when its column's group is
-    // its own (n >> 2 == t >> 1).  The accumulator columns 2t, 2t + 1 of lane t
-    // are digits (0, 1) for even t and (2, -) for odd t of group 2h + (t >> 1).
+    // MMA layout.  The chunk's 64 code bytes per row are four digit groups
+    // of 16 bytes.  For K half h and code class p, lane (g, t) holds the 8
+    // bytes 8 (t & 1) + [0, 8) of digit group G = 2 (t >> 1) + h of MMA rows
+    // g and g + 8 (MMA k = 4t + i <-> byte i, k = 16 + 4t + i <-> byte
+    // 4 + i of those 8), so an MMA covers groups h and 2 + h.  B column n is
+    // (local group n >> 2, digit n & 3), digit 3 unused: a lane's B registers
+    // are non-zero only when its column's group is its own (n >> 2 == t >> 1).
+    // The accumulator columns 2t, 2t + 1 of lane t are digits (0, 1) for even
+    // t and (2, -) for odd t of group G; a lane's two groups (h = 0, 1) are
+    // adjacent, so their scales and activation factors load together.
 
     // One-token units keep the B fragments of their digit slot in registers
-    // while the digit group stays the same.
-    uint2 bc[2][4];
-    int bc_key = -1;
+    // (one set per chunk of the item) while the digit groups stay the same.
+    uint2 bc[kItemChunks][2][4];
+    int bc_key[kItemChunks] = {-1, -1};
 
     __device__ __forceinline__ uint2 load_b(const uint8_t* __restrict__ dig, int slotdg, int h, int p,
                                             bool bActive) const {
         if (!bActive) return make_uint2(0u, 0u);
-        return lds64(dig + (slotdg + 2 * h + (t >> 1)) * kDgStride + (g & 3) * 64 + p * 16 + (t & 1) * 8);
+        return lds64(dig + (slotdg + 2 * (t >> 1) + h) * kDgStride + (g & 3) * 64 + p * 16 + (t & 1) * 8);
     }
 
-    // Tile rt of the current compute item (its slot at sp): exact group
-    // partial sums (a Horner chain per K half: D <<= 2 between code classes)
-    // -> per-row fp32 sums of the item's chunk into the batch's red buffer.
-    __device__ __forceinline__ void compute_tile(const unsigned char* sp, int rt, int tau, int c,
-                                                 const uint8_t* __restrict__ dig,
-                                                 const float2* __restrict__ fs) {
-        const int4 tile = T.tiles[tau];
-        const int ul = tile.x;
-        const int nT = T.units[ul].z;
-        const int nDG = W.Kd >> 6;
+    // Chunk ch of the current compute item (its slot at sp; chunk c of tile
+    // tau): exact group partial sums (a Horner chain per K half: D <<= 2
+    // between code classes) -> per-row fp32 sums into the batch's red buffer.
+    // (tile, nT, slot: the item's tile, its unit's pairs and their digit
+    // slots times the digit groups per vector, shared by the item's chunks.)
+    __device__ __forceinline__ void compute_chunk(const unsigned char* sp, int ch, int tau, int c,
+                                                  int nT, const int (&slot)[TMAX],
+                                                  const uint8_t* __restrict__ dig,
+                                                  const float2* __restrict__ fs) {
         const bool bActive = (g & 3) < 3 && (g >> 2) == (t >> 1);
-        const int rA = rt * 16 + g, rB = rA + 8;
+        const int rA = g, rB = g + 8;
         uint2 wa[2], wb[2];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            wa[h] = lds64(sp + rA * 64 + swz(rA, h) + 8 * t);
-            wb[h] = lds64(sp + rB * 64 + swz(rB, h) + 8 * t);
+            const int j = 4 * ch + 2 * (t >> 1) + h;
+            wa[h] = lds64(sp + swz(rA, j) + 8 * (t & 1));
+            wb[h] = lds64(sp + swz(rB, j) + 8 * (t & 1));
         }
         int slotdg[TMAX];
         int D[TMAX][2][4];
 #pragma unroll
         for (int j = 0; j < TMAX; ++j) {
-            const int slot = (j < nT) ? T.uslot[ul * TMAX + j] : 0;
-            slotdg[j] = slot * nDG + 4 * c;
+            slotdg[j] = slot[j] + 4 * c;
 #pragma unroll
             for (int h = 0; h < 2; ++h)
 #pragma unroll
                 for (int r = 0; r < 4; ++r) D[j][h][r] = 0;
         }
-        if (TMAX == 1 && bc_key != slotdg[0]) {
+        if (TMAX == 1 && bc_key[ch] != slotdg[0]) {
 #pragma unroll
             for (int h = 0; h < 2; ++h)
 #pragma unroll
-                for (int p = 0; p < 4; ++p) bc[h][p] = load_b(dig, slotdg[0], h, p, bActive);
-            bc_key = slotdg[0];
+                for (int p = 0; p < 4; ++p) bc[ch][h][p] = load_b(dig, slotdg[0], h, p, bActive);
+            bc_key[ch] = slotdg[0];
         }
 
 #pragma unroll
@@ -424,31 +456,40 @@ struct GemvPhase {
 #pragma unroll
                 for (int j = 0; j < TMAX; ++j) {
                     if (j < nT) {
-                        const uint2 bv = (TMAX == 1) ? bc[h][p] : load_b(dig, slotdg[j], h, p, bActive);
+                        const uint2 bv = (TMAX == 1) ? bc[ch][h][p] : load_b(dig, slotdg[j], h, p, bActive);
                         mma_u8s8(D[j][h], a0, a1, a2, a3, bv.x, bv.y);
                     }
                 }
             }
         }
 
-        // Even lanes finish row g, odd lanes row g + 8, of their group per K
-        // half; then the two lanes of a row with groups {t>>1, 2 + (t>>1)}
-        // add up across t ^ 2.
+        // Even lanes finish row g, odd lanes row g + 8, of their two groups;
+        // then lanes t and t ^ 2 add up the chunk's four groups:
+        // (G0 + G1) + (G2 + G3).
         const bool odd = t & 1;
-        const int row = odd ? rB : rA;
-        const uint16_t* s16 = reinterpret_cast<const uint16_t*>(sp + CODE_BYTES);
-        const uint16_t* b16 = s16 + ROWS * SPC;
+        const int srow = (tau - tfirst) * 16 + (odd ? g + 8 : g);  // the lane's row in the batch
+        const int nsb = W.Kd / GS;
+        const uint16_t* sb_s = sb;
+        const uint16_t* sb_b = sb + (size_t)sb_tiles * 16 * nsb;
         float sc[2], bi[2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int gi = (64 * (2 * h + (t >> 1))) / GS;
-            sc[h] = Half<DT>::to_f(s16[row * SPC + gi]);
-            bi[h] = Half<DT>::to_f(b16[row * SPC + gi]);
+        if (SPC == 4) {  // two adjacent groups' halves in one 4-byte load
+            const int si = srow * nsb + 4 * c + 2 * (t >> 1);
+            const uint32_t sv = *reinterpret_cast<const uint32_t*>(sb_s + si);
+            const uint32_t bv = *reinterpret_cast<const uint32_t*>(sb_b + si);
+            sc[0] = Half<DT>::to_f((uint16_t)(sv & 0xffffu));
+            sc[1] = Half<DT>::to_f((uint16_t)(sv >> 16));
+            bi[0] = Half<DT>::to_f((uint16_t)(bv & 0xffffu));
+            bi[1] = Half<DT>::to_f((uint16_t)(bv >> 16));
+        } else {  // gs = 128: both groups share one scale
+            const int si = srow * nsb + SPC * c + (t >> 1);
+            sc[0] = sc[1] = Half<DT>::to_f(sb_s[si]);
+            bi[0] = bi[1] = Half<DT>::to_f(sb_b[si]);
         }
         float* red_tile = red + (size_t)(tau - tfirst) * per_tile;
 #pragma unroll
         for (int j = 0; j < TMAX; ++j) {
             if (j < nT) {
+                const float4 fsv = *reinterpret_cast<const float4*>(fs + slotdg[j] + 2 * (t >> 1));
                 float part[2];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
@@ -459,8 +500,8 @@ struct GemvPhase {
                     const int d1 = odd ? s2 : cacc[1];
                     const int d2 = odd ? cacc[2] : s1;
                     const float v = fmaf((float)d0, 65536.f, fmaf((float)d1, 256.f, (float)d2));
-                    const float2 fsv = fs[slotdg[j] + 2 * h + (t >> 1)];
-                    part[h] = fmaf(sc[h], v * fsv.x, bi[h] * fsv.y);
+                    const float F = h ? fsv.z : fsv.x, S = h ? fsv.w : fsv.y;
+                    part[h] = fmaf(sc[h], v * F, bi[h] * S);
                 }
                 float pr = part[0] + part[1];
                 pr += __shfl_xor_sync(0xffffffffu, pr, 2);
@@ -472,38 +513,60 @@ struct GemvPhase {
     // Main loop (every thread calls it, after the warp's first DIST items
     // were issued): at each item the warp issues the item DIST ahead in its
     // sequence through `ahead()` (which may belong to the next phase), waits
-    // for its own current item and computes it.  Batches of `batch_tiles`
-    // tiles (a multiple of RT; the host makes one batch cover the phase when
-    // the red buffer allows) are each followed by the block-wide epilogue
-    // between two block barriers; the loads in flight keep streaming across.
+    // for its own current item and computes it.  Batches of sb_tiles tiles
+    // (the host makes one batch cover the phase when shared memory allows) start with a wait for their scales and biases and end
+    // with the block-wide epilogue between two block barriers, during which
+    // the next batch's scales and biases are issued; the loads in flight keep
+    // streaming across.  first_issued: the caller issued batch 0's scales and
+    // biases (issue_sb) already.  Returns false if a bounded wait gave up.
     template <class Out, class Ahead>
-    __device__ void consume(const uint8_t* dig, const float2* fs, float* red_base, int batch_tiles,
+    __device__ bool consume(const uint8_t* dig, const float2* fs, float* red_base, bool first_issued,
                             Out& out, Ahead& ahead) {
         red = red_base;
+        bool ok = true;
+        const int batch_tiles = sb_tiles;
+        if (!first_issued && T.ntiles > 0) issue_sb(0, min(T.ntiles, batch_tiles));
 #pragma unroll 1
         for (int tb0 = 0; tb0 < T.ntiles; tb0 += batch_tiles) {
             const int tb1 = min(T.ntiles, tb0 + batch_tiles);
             tfirst = tb0;
+            ok &= wait_sb();
 #pragma unroll 1
-            while (ci.n < count && ci.grp * RT < tb1) {
+            while (ci.n < count && ci.tile < tb1) {
                 ahead();
                 cp_async_wait<DIST>();
                 __syncwarp();
                 const unsigned char* sp = ring + ((q0 + ci.n) % STAGES) * SLOT;
+                const int ul = T.tiles[ci.tile].x;
+                const int nT = (TMAX == 1) ? 1 : T.units[ul].z;
+                int slot[TMAX];
 #pragma unroll
-                for (int rt = 0; rt < RT; ++rt) {
-                    const int tau = ci.grp * RT + rt;
-                    if (tau < T.ntiles) compute_tile(sp, rt, tau, ci.c, dig, fs);
+                for (int j = 0; j < TMAX; ++j) slot[j] = ((j < nT) ? T.uslot[ul * TMAX + j] : 0) * (W.Kd >> 6);
+#pragma unroll
+                for (int ch = 0; ch < kItemChunks; ++ch) {
+                    const int c = kItemChunks * ci.cp + ch;
+                    if (c < nK) compute_chunk(sp, ch, ci.tile, c, nT, slot, dig, fs);
                 }
                 __syncwarp();
                 advance(ci);
             }
             bar_sync(kBarConsumers, kConsumerThreads);
+            if (tb1 < T.ntiles) issue_sb(tb1, min(T.ntiles, tb1 + batch_tiles));
             epilogue_tiles<TMAX, MODE>(tb0, tb1, red_base, nK, T.tiles, T.units, out);
             bar_sync(kBarConsumers, kConsumerThreads);
         }
+        return ok;
     }
 };
+
+// Thread 0: initialises a phase's scale/bias mbarrier (one cp.async arrival
+// per thread and batch); the block synchronises before its first use.
+__device__ __forceinline__ void sb_init(uint64_t* bar) {
+    if (threadIdx.x == 0) {
+        mbar_init(bar, kConsumerThreads);
+        mbar_fence_init();
+    }
+}
 
 // Before the block exits, wait until every cp.async this thread issued has
 // landed, so no copy is still writing into shared memory.

@@ -277,6 +277,7 @@ template <int DT, int GS, int TMAX, int STAGES>
 __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const LayerArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ int s_nunits, s_bad, s_flag, s_nlast, s_nseg;
+    __shared__ __align__(8) uint64_t s_sbar_up, s_sbar_dn;
     __shared__ int s_cnt_up[4], s_cnt_dn[4];
     __shared__ int s_last[kLayerMaxLastBlocks];
     __shared__ int2 s_seg[kLayerMaxLastBlocks];
@@ -365,10 +366,17 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
 
     const PhaseWeights up_w{a.w_ug, a.s_ug, a.b_ug, 2 * a.I, a.I, a.H};
     const PhaseWeights dn_w{a.w_dn, a.s_dn, a.b_dn, a.H, 0, a.I};
+    // one scale/bias buffer: the down phase's first batch is issued once the
+    // up phase's last batch is computed
+    uint16_t* s_sb = reinterpret_cast<uint16_t*>(smem + a.off_sb);
+    sb_init(&s_sbar_up);
+    sb_init(&s_sbar_dn);
     const PhaseTables up_tabs{up_tb.tiles, up_tb.lunits, up_tb.uslot, s_cnt_up[0]};
-    GemvPhase<DT, GS, kModeUpSwiglu, TMAX, STAGES> up(up_tabs, up_w, s_ring, 0, a.nK_up);
+    GemvPhase<DT, GS, kModeUpSwiglu, TMAX, STAGES> up(up_tabs, up_w, s_ring, 0, a.nK_up, s_sb, a.batch_up,
+                                                      &s_sbar_up);
     const PhaseTables dn_tabs{dn_tb.tiles, dn_tb.lunits, dn_tb.uslot, s_cnt_dn[0]};
-    GemvPhase<DT, GS, kModeRows, TMAX, STAGES> dn(dn_tabs, dn_w, s_ring, up.count, a.nK_dn);
+    GemvPhase<DT, GS, kModeRows, TMAX, STAGES> dn(dn_tabs, dn_w, s_ring, up.count, a.nK_dn, s_sb, a.batch_dn,
+                                                  &s_sbar_dn);
 
     // One item sequence per warp: its up items, then its down items, which
     // start streaming during the up phase's last items.
@@ -378,6 +386,8 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
     };
     auto ahead_dn = [&]() { dn.load_next(); };
     __syncthreads();  // tables
+    // the first batch's scales and biases go out before the first code items
+    if (s_cnt_up[0] > 0) up.issue_sb(0, min(s_cnt_up[0], a.batch_up));
     up.prefetch(ahead_up);
 
     // ---- 2. up||gate phase --------------------------------------------------
@@ -390,14 +400,17 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
     }
     {
         ActOut<DT, TMAX> out{up_tb.upair, a.act, a.I, a.clamp};
-        up.consume(s_dig, s_fs, s_red, a.batch_up, out, ahead_up);
+        if (!up.consume(s_dig, s_fs, s_red, true, out, ahead_up) && tid == 0)
+            atomicExch(a.ctrl + kCtrlError, MOMIJ_ERR_TIMEOUT);
     }
+    if (s_cnt_dn[0] > 0) dn.issue_sb(0, min(s_cnt_dn[0], a.batch_dn));  // lands during the grid barrier
     stamp(a, 6);
     stamp(a, 7);
 
     // ---- 3/4. down phase: its stages are already streaming --------------------
     if (!grid_barrier(a.ctrl_u + kCtrlBarrier, a.ctrl + kCtrlError, &s_flag)) {
-        ring_quiesce();  // the down stages issued before the barrier
+        ring_quiesce();  // the down items issued before the barrier
+        if (s_cnt_dn[0] > 0) dn.wait_sb();
         return;
     }
     stamp(a, 8);
@@ -406,7 +419,8 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
     stamp(a, 9);
     {
         DownOut<DT, TMAX> out{dn_tb.upair, a.down, a.H};
-        dn.consume(s_dig, s_fs, s_red, a.batch_dn, out, ahead_dn);
+        if (!dn.consume(s_dig, s_fs, s_red, true, out, ahead_dn) && tid == 0)
+            atomicExch(a.ctrl + kCtrlError, MOMIJ_ERR_TIMEOUT);
     }
     ring_quiesce();
     __threadfence();  // down rows written by this thread, before the block counters below

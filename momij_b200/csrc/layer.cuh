@@ -40,14 +40,15 @@ struct LayerArgs {
     int route_parts;  // threads per candidate of the rank top-k (a power of two dividing E), 0: per-warp rounds
     float clamp;
     int nK_up, nK_dn;        // 256-code chunks per row of each phase
-    int batch_up, batch_dn;  // tiles per epilogue batch of each phase (multiples of item_tiles)
+    int batch_up, batch_dn;  // tiles per epilogue batch of each phase (multiples of item_tiles):
+                             // red and scale buffers, shared by the phases
     int max_tiles, max_units, max_vec;  // capacities of the shared-memory tables
     long long* trace;  // optional: kTracePoints %globaltimer stamps per CTA (thread 0)
     // dynamic shared-memory carve-up (byte offsets)
     int off_logits, off_inds, off_scores, off_sorted, off_pflag, off_units;
     int off_tiles_up, off_lunits_up, off_upair_up, off_uslot_up, off_seg_up, off_xvecs;
     int off_tiles_dn, off_lunits_dn, off_upair_dn, off_uslot_dn, off_seg_dn, off_vecs_dn;
-    int off_fs, off_dig, off_red, off_stage;
+    int off_fs, off_dig, off_red, off_sb, off_stage;
 };
 
 template <int DT, int GS, int TMAX, int STAGES>
