@@ -381,7 +381,7 @@ def run_gpu(args, cfg) -> None:
     tf = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tf):
         try:
-            traffic = json.load(open(tf)).get(args.config, {}).get("up_bytes_per_launch")
+            traffic = json.load(open(tf)).get(args.config, {}).get("traffic_bytes_per_launch")
         except Exception:
             traffic = None
 

@@ -203,10 +203,10 @@ using LayerFn = void (*)(const LayerArgs);
 template <int DT, int GS>
 LayerFn pick_layer_tm(int tmax) {
     switch (tmax) {
-        case 1: return moe_layer_kernel<DT, GS, 1, kLayerStages>;
-        case 2: return moe_layer_kernel<DT, GS, 2, kLayerStages>;
-        case 4: return moe_layer_kernel<DT, GS, 4, kLayerStages>;
-        default: return moe_layer_kernel<DT, GS, 8, kLayerStages>;
+        case 1: return moe_layer_kernel<DT, GS, 1, layer_stages(1)>;
+        case 2: return moe_layer_kernel<DT, GS, 2, layer_stages(2)>;
+        case 4: return moe_layer_kernel<DT, GS, 4, layer_stages(4)>;
+        default: return moe_layer_kernel<DT, GS, 8, layer_stages(8)>;
     }
 }
 LayerFn pick_layer(int dtype, int gs, int tmax) {
@@ -243,7 +243,7 @@ int run_fused_layer(LayerArgs a, int dtype, int gs, const Workspace& ws, cudaStr
     if (!fused_enabled() || a.M > 8 || P > kLayerMaxPairs || a.E > 1024 || a.K > 32)
         return kNotApplicable;
     const int tmax = pick_tmax(a.M);
-    const int stages = kLayerStages;
+    const int stages = layer_stages(tmax);
     const int rt = item_tiles(tmax);
     const int G = current_device_sm_count();
     if (G <= 0) return kNotApplicable;
@@ -302,7 +302,8 @@ int run_fused_layer(LayerArgs a, int dtype, int gs, const Workspace& ws, cudaStr
         const size_t ring = (size_t)kConsumerWarps * stages * slot_bytes(tmax);
         if (off + ring + 256 > limit) return kNotApplicable;
         const size_t avail = limit - off - ring - 256;
-        const size_t rpt_up = 4 * (size_t)a.nK_up * tmax * 16, rpt_dn = 4 * (size_t)a.nK_dn * tmax * 16;
+        const size_t rpt_up = 4 * (size_t)((a.nK_up + 1) / 2) * tmax * 16,
+                     rpt_dn = 4 * (size_t)((a.nK_dn + 1) / 2) * tmax * 16;  // red_floats_per_tile
         const size_t spt_up = sb_bytes_per_tile(a.H, gs), spt_dn = sb_bytes_per_tile(a.I, gs);
         size_t bu = (size_t)(mt_up + rt - 1) / rt * rt, bd = (size_t)(mt_dn + rt - 1) / rt * rt;
         auto need = [&]() {
@@ -417,7 +418,7 @@ bool configure_gemv(GemvLaunch& L, int mode, int tmax, int gs) {
 
     const size_t limit = (size_t)max_dyn_smem();
     const int rt = item_tiles(tmax);
-    const size_t pt = 4 * (size_t)nK * tmax * 16;  // red_floats_per_tile
+    const size_t pt = 4 * (size_t)((nK + 1) / 2) * tmax * 16;  // red_floats_per_tile
     for (int stages : {4, 2}) {
         size_t off = 0;
         a.off_tiles = (int)off; off += 16 * (size_t)a.max_tiles;

@@ -151,23 +151,24 @@ __host__ __device__ constexpr int slot_bytes(int) { return 16 * 128; }
 // biases (halves); MMA row r of the batch's tile k at row 16 k + r.
 __host__ __device__ constexpr int sb_bytes_per_tile(int Kd, int gs) { return 16 * (Kd / gs) * 2 * 2; }
 
-// Red-buffer floats per tile: [nK][TMAX][16 rows], each the sum of the four
-// lane groups' partials of one chunk, (t0 + t1) + (t2 + t3).
+// Red-buffer floats per tile: [chunk pairs][TMAX][16 rows], each the sum of
+// one item's two chunks (chunk 2cp, then + chunk 2cp + 1), a chunk's value
+// being ((G0 + G1) + (G2 + G3)) over its four digit groups.
 template <int TMAX>
-__host__ __device__ constexpr int red_floats_per_tile(int nK) { return nK * TMAX * 16; }
+__host__ __device__ constexpr int red_floats_per_tile(int nK) { return ((nK + 1) / 2) * TMAX * 16; }
 // Sum of the partials of MMA row r (0..15) of token slot j of one tile over
-// all chunks, computed by L lanes (an aligned group; L = 1, 2, 4 or 8; lane
+// its n entries (chunk pairs), computed by L lanes (an aligned group; L = 1, 2, 4 or 8; lane
 // `sub` of the group).  The association is fixed whatever L is:
 // with S_v the sequential sum of the chunk values v, v + 8, ... (v = 0..7),
 // the result is ((S0 + S1) + (S2 + S3)) + ((S4 + S5) + (S6 + S7)).
 template <int TMAX, int L>
-__device__ __forceinline__ float tile_sum(const float* red, int nK, int j, int r, int sub) {
+__device__ __forceinline__ float tile_sum(const float* red, int n, int j, int r, int sub) {
     constexpr int V = 8 / L;
     float part[V];
 #pragma unroll
     for (int v = 0; v < V; ++v) {
         float acc = 0.f;
-        for (int cc = sub * V + v; cc < nK; cc += 8) acc += red[(cc * TMAX + j) * 16 + r];
+        for (int cc = sub * V + v; cc < n; cc += 8) acc += red[(cc * TMAX + j) * 16 + r];
         part[v] = acc;
     }
 #pragma unroll
@@ -205,8 +206,9 @@ __device__ void epilogue_tiles(int tfirst, int tlast, const float* red_base, int
             valid = j < units[tile.x].z && r < tile.z;
         }
         const float* red = red_base + (size_t)(tau - tfirst) * per_tile;
-        const float v = tile_sum<TMAX, 8>(red, nK, j, r, sub);
-        const float vg = (MODE == kModeUpSwiglu) ? tile_sum<TMAX, 8>(red, nK, j, 8 + r, sub) : 0.f;
+        const int ncp = (nK + 1) / 2;
+        const float v = tile_sum<TMAX, 8>(red, ncp, j, r, sub);
+        const float vg = (MODE == kModeUpSwiglu) ? tile_sum<TMAX, 8>(red, ncp, j, 8 + r, sub) : 0.f;
         if (valid && sub == 0) out(tile, j, r, v, vg);
     }
 }
@@ -404,13 +406,14 @@ struct GemvPhase {
 
     // Chunk ch of the current compute item (its slot at sp; chunk c of tile
     // tau): exact group partial sums (a Horner chain per K half: D <<= 2
-    // between code classes) -> per-row fp32 sums into the batch's red buffer.
+    // between code classes) -> per-row fp32 sums, set (ch 0) or added (ch 1)
+    // into acc[j] of lanes t < 2 (row g for t = 0, g + 8 for t = 1).
     // (tile, nT, slot: the item's tile, its unit's pairs and their digit
     // slots times the digit groups per vector, shared by the item's chunks.)
     __device__ __forceinline__ void compute_chunk(const unsigned char* sp, int ch, int tau, int c,
                                                   int nT, const int (&slot)[TMAX],
                                                   const uint8_t* __restrict__ dig,
-                                                  const float2* __restrict__ fs) {
+                                                  const float2* __restrict__ fs, float (&acc)[TMAX]) {
         const bool bActive = (g & 3) < 3 && (g >> 2) == (t >> 1);
         const int rA = g, rB = g + 8;
         uint2 wa[2], wb[2];
@@ -485,7 +488,6 @@ struct GemvPhase {
             sc[0] = sc[1] = Half<DT>::to_f(sb_s[si]);
             bi[0] = bi[1] = Half<DT>::to_f(sb_b[si]);
         }
-        float* red_tile = red + (size_t)(tau - tfirst) * per_tile;
 #pragma unroll
         for (int j = 0; j < TMAX; ++j) {
             if (j < nT) {
@@ -505,7 +507,7 @@ struct GemvPhase {
                 }
                 float pr = part[0] + part[1];
                 pr += __shfl_xor_sync(0xffffffffu, pr, 2);
-                if (t < 2) red_tile[(c * TMAX + j) * 16 + t * 8 + g] = pr;
+                acc[j] = ch ? acc[j] + pr : pr;
             }
         }
     }
@@ -542,10 +544,17 @@ struct GemvPhase {
                 int slot[TMAX];
 #pragma unroll
                 for (int j = 0; j < TMAX; ++j) slot[j] = ((j < nT) ? T.uslot[ul * TMAX + j] : 0) * (W.Kd >> 6);
+                float acc[TMAX];
 #pragma unroll
                 for (int ch = 0; ch < kItemChunks; ++ch) {
                     const int c = kItemChunks * ci.cp + ch;
-                    if (c < nK) compute_chunk(sp, ch, ci.tile, c, nT, slot, dig, fs);
+                    if (c < nK) compute_chunk(sp, ch, ci.tile, c, nT, slot, dig, fs, acc);
+                }
+                float* red_tile = red + (size_t)(ci.tile - tfirst) * per_tile;
+                if (t < 2) {
+#pragma unroll
+                    for (int j = 0; j < TMAX; ++j)
+                        if (j < nT) red_tile[(ci.cp * TMAX + j) * 16 + t * 8 + g] = acc[j];
                 }
                 __syncwarp();
                 advance(ci);

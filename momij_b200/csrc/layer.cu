@@ -486,11 +486,11 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
 
 #define MOMIJ_LAYER_INST(DT, GS, TM, ST) \
     template __global__ void moe_layer_kernel<DT, GS, TM, ST>(const LayerArgs);
-#define MOMIJ_LAYER_INST_TM(DT, GS)           \
-    MOMIJ_LAYER_INST(DT, GS, 1, kLayerStages) \
-    MOMIJ_LAYER_INST(DT, GS, 2, kLayerStages) \
-    MOMIJ_LAYER_INST(DT, GS, 4, kLayerStages) \
-    MOMIJ_LAYER_INST(DT, GS, 8, kLayerStages)
+#define MOMIJ_LAYER_INST_TM(DT, GS)               \
+    MOMIJ_LAYER_INST(DT, GS, 1, layer_stages(1)) \
+    MOMIJ_LAYER_INST(DT, GS, 2, layer_stages(2)) \
+    MOMIJ_LAYER_INST(DT, GS, 4, layer_stages(4)) \
+    MOMIJ_LAYER_INST(DT, GS, 8, layer_stages(8))
 MOMIJ_LAYER_INST_TM(MOMIJ_DTYPE_BF16, 64)
 MOMIJ_LAYER_INST_TM(MOMIJ_DTYPE_BF16, 128)
 MOMIJ_LAYER_INST_TM(MOMIJ_DTYPE_F16, 64)

@@ -13,7 +13,10 @@ constexpr int kCtrlStatus = 1, kCtrlError = 2, kCtrlBarrier = 3;
 constexpr int kLayerMaxLastBlocks = 64;
 constexpr int kLayerThreads = 512;  // 16 warps that load and compute
 constexpr int kLayerMaxPairs = 64;
-constexpr int kLayerStages = 4;  // ring slots per warp (items in flight + 1)
+// Ring slots per warp (items in flight + 1): one- and two-token units are
+// memory-bound and keep 3 items in flight; larger units are compute-bound and
+// need the shared memory for their tokens' digit planes.
+__host__ __device__ constexpr int layer_stages(int tmax) { return tmax <= 2 ? 4 : 2; }
 constexpr int kTracePoints = 16;  // phase stamps per CTA when tracing (momij_layer_trace)
 
 struct LayerArgs {
