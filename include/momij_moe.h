@@ -54,6 +54,9 @@ enum momij_status {
 enum momij_dtype { MOMIJ_DTYPE_BF16 = 0, MOMIJ_DTYPE_F16 = 1 };
 
 #define MOMIJ_MAX_PAIRS 1024
+/* momij_moe_expert_ffn / momij_moe_forward: M*Ktop up to this many pairs
+ * through the grouped (prefill) path. */
+#define MOMIJ_MAX_GROUPED_PAIRS 65536
 
 /* Human-readable name of a status code (never NULL). */
 const char* momij_status_string(int status);

@@ -14,6 +14,7 @@
 #include "kernels.cuh"
 #include "gemv_core.cuh"
 #include "layer.cuh"
+#include "prefill.cuh"
 
 using namespace momij;
 
@@ -140,8 +141,13 @@ struct Workspace {
     int32_t* inds;
     float* scores;
     unsigned* block_ctr;
+    int32_t* grp;  // grouped path: offsets [1025], pair [P], weight [P] (float), block list (16-B aligned)
     size_t bytes;
 };
+
+// Grouped-path tables in the workspace (sized for up to kGrpMaxExperts experts).
+constexpr int kGrpMaxExperts = 1024;
+constexpr size_t kGrpOffsets = kGrpMaxExperts + 1;
 
 size_t plan_bytes(int P) { return align_up(sizeof(int32_t) * (kPlanHeader + 5 * (size_t)P), 256); }
 
@@ -162,6 +168,8 @@ Workspace carve(void* ws, int M, int Ktop, int H, int I) {
     off += align_up(P * 4, 256);
     w.block_ctr = reinterpret_cast<unsigned*>(p + off);
     off += align_up((size_t)((H + 63) / 64) * 4, 256);
+    w.grp = reinterpret_cast<int32_t*>(p + off);
+    off += align_up(4 * (kGrpOffsets + 2 * P + 4 + block_list_ints((int)P, kGrpMaxExperts)), 256);
     w.bytes = off;
     return w;
 }
@@ -546,6 +554,82 @@ int check_device() {
     return MOMIJ_OK;
 }
 
+// ---- grouped (prefill) path: permute + tcgen05 grouped GEMMs + combine ------
+bool grouped_enabled(int M, int Ktop, int E) {
+    const char* v = std::getenv("MOMIJ_GROUPED");
+    if (v && v[0] == '0') return (long long)M * Ktop > MOMIJ_MAX_PAIRS;  // forced off unless required
+    if (v && v[0] == '1') return M > 8;
+    // tokens per expert large enough for the weights to be re-used across tokens
+    return M > 8 && ((long long)M * Ktop >= 32LL * E || (long long)M * Ktop > MOMIJ_MAX_PAIRS);
+}
+
+using GroupedFn = void (*)(const GroupedArgs);
+template <int DT, int GS>
+GroupedFn pick_grouped_dt(int mode) {
+    return mode == kModeUpSwiglu ? grouped_gemm_kernel<DT, GS, kModeUpSwiglu> : grouped_gemm_kernel<DT, GS, kModeRows>;
+}
+GroupedFn pick_grouped(int dtype, int gs, int mode) {
+    if (dtype == MOMIJ_DTYPE_BF16)
+        return gs == 64 ? pick_grouped_dt<MOMIJ_DTYPE_BF16, 64>(mode) : pick_grouped_dt<MOMIJ_DTYPE_BF16, 128>(mode);
+    return gs == 64 ? pick_grouped_dt<MOMIJ_DTYPE_F16, 64>(mode) : pick_grouped_dt<MOMIJ_DTYPE_F16, 128>(mode);
+}
+
+int run_grouped(const void* x, const uint32_t* w_ug, const void* s_ug, const void* b_ug,
+                const uint32_t* w_dn, const void* s_dn, const void* b_dn, const int32_t* inds,
+                const float* scores, void* y, void* resid_h, int M, int H, int I, int E, int Ktop,
+                int gs, float clamp, int dtype, const Workspace& ws, cudaStream_t st) {
+    if (E > kGrpMaxExperts || I % 64 || H % 128) return MOMIJ_ERR_UNSUPPORTED_SHAPE;
+    const int P = M * Ktop;
+    // status words: the work-plan header ([1] routing status, [2] sticky error
+    // word), as for the other paths (combine_kernel, momij_moe_synchronize)
+    int32_t* hdr = ws.plan;
+    int32_t* offsets = ws.grp;
+    int32_t* pair = offsets + kGrpOffsets;
+    float* weight = reinterpret_cast<float*>(pair + P);
+    // the block list is read as int4 entries: 16-byte aligned (the region has 4 ints of slack)
+    int32_t* blocks = reinterpret_cast<int32_t*>(align_up(reinterpret_cast<uintptr_t>(weight + P), 16));
+    if (cudaMemsetAsync(hdr + 1, 0, sizeof(int32_t), st) != cudaSuccess) return MOMIJ_ERR_CUDA;
+    int slot = prof_begin(MOMIJ_KERNEL_PLAN, st);
+    int rc = cuda_status(launch(permute_kernel, dim3(1), dim3(1024), sizeof(int) * (E + 1), st, inds,
+                                scores, P, E, offsets, pair, weight, hdr + 1));
+    if (!rc) rc = cuda_status(launch(block_list_kernel, dim3(1), dim3(32), 0, st,
+                                     static_cast<const int32_t*>(offsets), E, blocks,
+                                     static_cast<const int32_t*>(hdr + 1)));
+    prof_end(slot, st);
+    if (rc) return rc;
+    const int G = current_device_sm_count();
+    if (G <= 0) return MOMIJ_ERR_CUDA;
+    const size_t smem = 2 * (2 * 128 * 128 + kBlockTokens * 128) + 1024;  // 2 stages x (A hi, A lo, B)
+    for (int mode : {kModeUpSwiglu, kModeRows}) {
+        GroupedArgs a{};
+        a.x = static_cast<const uint16_t*>(mode == kModeUpSwiglu ? x : ws.act);
+        a.x_per_pair = mode == kModeUpSwiglu ? 0 : 1;
+        a.w = mode == kModeUpSwiglu ? w_ug : w_dn;
+        a.s = static_cast<const uint16_t*>(mode == kModeUpSwiglu ? s_ug : s_dn);
+        a.b = static_cast<const uint16_t*>(mode == kModeUpSwiglu ? b_ug : b_dn);
+        a.blocks = blocks;
+        a.pairs = pair;
+        a.status = hdr;
+        a.out = mode == kModeUpSwiglu ? ws.act : ws.down;
+        a.Kd = mode == kModeUpSwiglu ? H : I;
+        a.N = mode == kModeUpSwiglu ? 2 * I : H;
+        a.Ru = mode == kModeUpSwiglu ? I : 0;
+        a.Ktop = Ktop;
+        a.clamp = clamp;
+        a.E = E;
+        a.P = P;
+        GroupedFn fn = pick_grouped(dtype, gs, mode);
+        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return MOMIJ_ERR_CUDA;
+        slot = prof_begin(mode == kModeUpSwiglu ? MOMIJ_KERNEL_UP : MOMIJ_KERNEL_ROWS, st);
+        rc = cuda_status(launch(fn, dim3(G), dim3(kGroupedThreads), smem, st, a));
+        prof_end(slot, st);
+        if (rc) return rc;
+    }
+    return launch_combine_dt(dtype, ws.down, scores, static_cast<uint16_t*>(resid_h ? resid_h : y), M,
+                             Ktop, H, resid_h != nullptr, hdr, st);
+}
+
 // Shared body of expert_ffn and forward once inds/scores/plan are enqueued.
 int ffn_after_plan(const void* x, const uint32_t* w_ug, const void* s_ug, const void* b_ug,
                    const uint32_t* w_dn, const void* s_dn, const void* b_dn, const float* scores,
@@ -780,7 +864,9 @@ static int validate_ffn(const void* x, const uint32_t* w_ug, const void* s_ug, c
         !workspace || M < 0 || Ktop < 1 || E < 1 ||
         (dtype != MOMIJ_DTYPE_BF16 && dtype != MOMIJ_DTYPE_F16))
         return MOMIJ_ERR_INVALID_ARGUMENT;
-    if (!shape_ok(H, gs) || !shape_ok(I, gs) || (long long)M * Ktop > MOMIJ_MAX_PAIRS)
+    if (!shape_ok(H, gs) || !shape_ok(I, gs) || (long long)M * Ktop > MOMIJ_MAX_GROUPED_PAIRS)
+        return MOMIJ_ERR_UNSUPPORTED_SHAPE;
+    if ((long long)M * Ktop > MOMIJ_MAX_PAIRS && (E > kGrpMaxExperts || I % 64 || H % 128))
         return MOMIJ_ERR_UNSUPPORTED_SHAPE;
     if (!aligned(x, 16) || !aligned(w_ug, 16) || !aligned(w_dn, 16) || !aligned(s_ug, 8) ||
         !aligned(b_ug, 8) || !aligned(s_dn, 8) || !aligned(b_dn, 8) || !aligned(workspace, 256))
@@ -803,6 +889,9 @@ int momij_moe_expert_ffn(const void* x, const uint32_t* w_ug, const void* s_ug, 
     if (M == 0) return MOMIJ_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     Workspace ws = carve(workspace, M, Ktop, H, I);
+    if (grouped_enabled(M, Ktop, E))
+        return run_grouped(x, w_ug, s_ug, b_ug, w_dn, s_dn, b_dn, inds, scores, y, resid_h, M, H, I, E,
+                           Ktop, gs, clamp, dtype, ws, st);
     LayerArgs la = layer_args(nullptr, inds, scores, nullptr, nullptr, x, w_ug, s_ug, b_ug, w_dn,
                               s_dn, b_dn, y, resid_h, M, H, I, E, Ktop, clamp);
     const int frc = run_fused_layer(la, dtype, gs, ws, st);
@@ -831,6 +920,16 @@ int momij_moe_forward(const float* logits, const void* x, const uint32_t* w_ug, 
     Workspace ws = carve(workspace, M, Ktop, H, I);
     int32_t* ind_out = inds ? inds : ws.inds;
     float* sc_out = scores ? scores : ws.scores;
+    if (grouped_enabled(M, Ktop, E)) {
+        const int slot = prof_begin(MOMIJ_KERNEL_PLAN, st);
+        const int warps = 8;
+        int rc = cuda_status(launch(route_kernel, dim3((M + warps - 1) / warps), dim3(32 * warps), 0, st,
+                                    logits, M, E, Ktop, ind_out, sc_out));
+        prof_end(slot, st);
+        if (rc) return rc;
+        return run_grouped(x, w_ug, s_ug, b_ug, w_dn, s_dn, b_dn, ind_out, sc_out, y, resid_h, M, H, I,
+                           E, Ktop, gs, clamp, dtype, ws, st);
+    }
     LayerArgs la = layer_args(logits, nullptr, nullptr, ind_out, sc_out, x, w_ug, s_ug, b_ug, w_dn,
                               s_dn, b_dn, y, resid_h, M, H, I, E, Ktop, clamp);
     const int frc = run_fused_layer(la, dtype, gs, ws, st);

@@ -1,0 +1,332 @@
+// prefill.cu -- grouped GEMM of the 2-bit experts on the tcgen05 tensor cores
+// for prefill / large verify batches (tokens per expert large enough that the
+// weights are re-used across tokens).
+//
+// Per tile (one block of <= 128 sorted pairs of one expert x 128 weight rows):
+//   D[row, token] = sum_k dequant(W[e])[row, k] * X[token, k]
+// with D (fp32) in tensor memory.  Each k-block of 64 elements is staged in
+// shared memory as K-major 128-byte-swizzled tiles: the 128 weight rows
+// dequantised (w = s*q + b in fp32) and split into two activation-dtype tiles
+// A_hi = round(w) and A_lo = round(w - A_hi), so A_hi + A_lo carries w to
+// ~2^-17 (a single 16-bit rounding of w would cost ~2^-9 per weight, several
+// times the tolerance after two projections); B = the block's token rows
+// gathered with cp.async.  One thread issues eight tcgen05.mma.kind::f16
+// (M=128, N=tokens rounded up to 16, K=16; hi then lo into the same fp32
+// accumulator) per k-block and commits them to the stage's mbarrier; the
+// other threads fill the other stage meanwhile.  The epilogue reads TMEM (tcgen05.ld) and writes per-pair
+// rows: the staged clamped SwiGLU of up||gate (tile = 64 up rows + the
+// matching 64 gate rows), or the down projection.
+//
+// Reference semantics: MLX gatherQuantizedMM for M*Ktop rows (MapleMoE.swift:
+// 65-75) with sortedIndices false; the grouping by expert is this build's
+// (the reference reuses its GEMV for prefill, SeedlessDecodeEngine.swift:
+// 516-545).  Outputs are per (token, slot) pair like gqmm2, so the same
+// combine kernel applies.
+#include "common.cuh"
+#include "prefill.cuh"
+
+namespace momij {
+
+namespace {
+
+constexpr int kStageA = 128 * 128;           // 128 weight rows x 64 elements x 2 B (one of hi / lo)
+constexpr int kStageB = kBlockTokens * 128;  // tokens x 64 elements x 2 B
+constexpr int kStageBytes = 2 * kStageA + kStageB;
+constexpr int kStages = 2;
+constexpr int kTmemCols = kBlockTokens;      // fp32 accumulator columns
+constexpr int kMmaWaitLimit = 1 << 24;
+
+// tcgen05 shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row
+// groups 1024 B apart (leading byte offset unused for swizzled K-major).
+__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor, kind::f16: fp32 D, A and B bf16 (or f16), both
+// K-major, M = 128, N = n.
+template <int DT>
+__device__ __forceinline__ uint32_t idesc_f16(int n) {
+    const uint32_t ab = (DT == MOMIJ_DTYPE_BF16) ? 1u : 0u;
+    return (1u << 4) | (ab << 7) | (ab << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+// Byte offset of element (r, k), k < 64, in a K-major tile with 128-byte
+// rows and 128-byte swizzle (16-byte chunk c of row r at c ^ (r & 7)).
+__device__ __forceinline__ uint32_t sw128(int r, int k) {
+    return (r >> 3) * 1024 + (r & 7) * 128 + ((((k * 2) >> 4) ^ (r & 7)) << 4) + ((k * 2) & 15);
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Two fp32 values -> two activation-dtype values packed (first in the low half).
+template <int DT>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+    uint32_t r;
+    if (DT == MOMIJ_DTYPE_BF16)
+        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    else
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+        "[%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+          "=r"(v[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+}  // namespace
+
+__global__ void block_list_kernel(const int32_t* offsets, int E, int32_t* blocks, const int32_t* status) {
+    const int lane = threadIdx.x & 31;
+    pdl_wait();  // offsets and status are written by permute_kernel
+    if (threadIdx.x >= 32) return;
+    if (status && *status != MOMIJ_OK) {
+        if (lane == 0) blocks[0] = 0;
+        return;
+    }
+    int carry = 0;
+    for (int base = 0; base < E; base += 32) {
+        const int e = base + lane;
+        const int lo = e < E ? offsets[e] : 0, hi = e < E ? offsets[e + 1] : 0;
+        const int nb = (hi - lo + kBlockTokens - 1) / kBlockTokens;
+        int incl = nb;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const int first = carry + incl - nb;
+        for (int j = 0; j < nb; ++j) {
+            int32_t* ent = blocks + kBlockHeader + 4 * (first + j);
+            ent[0] = e;
+            ent[1] = lo + j * kBlockTokens;
+            ent[2] = min(kBlockTokens, hi - lo - j * kBlockTokens);
+            ent[3] = 0;
+        }
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) blocks[0] = carry;
+    pdl_launch_dependents();
+}
+
+template <int DT, int GS, int MODE>
+__global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const GroupedArgs a) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* smem =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint32_t s_tmem;
+    __shared__ __align__(8) uint64_t s_bar[kStages];
+    __shared__ int s_pair[kBlockTokens], s_row[kBlockTokens];
+    __shared__ int s_timeout;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    pdl_wait();
+    if (a.status[1] != MOMIJ_OK || a.status[2] != MOMIJ_OK) return;
+    const int nblocks = a.blocks[0];
+    if (nblocks < 0 || nblocks > a.P / kBlockTokens + a.E + 1) {  // cannot come from block_list_kernel
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(a.status + 2, MOMIJ_ERR_WORKSPACE);
+        return;
+    }
+    const int nrb = (MODE == kModeUpSwiglu) ? a.Ru / 64 : a.N / 128;
+    const int ntiles = nblocks * nrb;
+    if ((int)blockIdx.x >= ntiles) return;
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) mbar_init(&s_bar[s], 1);
+        mbar_fence_init();
+        s_timeout = 0;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    uint32_t phase[kStages] = {0u, 0u};
+    bool pending[kStages] = {false, false};
+    auto wait_stage = [&](int s) {
+        bool ok = false;
+        for (int it = 0; it < kMmaWaitLimit && !ok; ++it) ok = mbar_try_wait(&s_bar[s], phase[s]);
+        if (!ok) s_timeout = 1;
+        phase[s] ^= 1u;
+        pending[s] = false;
+    };
+
+    const int KB = a.Kd / 64;
+    const int nsb = a.Kd / GS;
+    const int ra = tid >> 1, half = tid & 1;  // this thread dequantises row ra, codes half*32 + [0, 32)
+    const int4* blist = reinterpret_cast<const int4*>(a.blocks + kBlockHeader);
+
+#pragma unroll 1
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        const int bi = t / nrb, rb = t - bi * nrb;
+        const int4 blk = blist[bi];
+        const int e = blk.x, start = blk.y, cnt = blk.z;
+        // a malformed entry (it cannot come from block_list_kernel) is an error, not an access
+        if (e < 0 || e >= a.E || start < 0 || cnt < 1 || cnt > kBlockTokens || start + cnt > a.P) {
+            if (tid == 0) atomicExch(a.status + 2, MOMIJ_ERR_WORKSPACE);
+            continue;
+        }
+        const int nmma = (cnt + 15) & ~15;
+        if (tid < kBlockTokens) {
+            const int p = tid < cnt ? min(max(a.pairs[start + tid], 0), a.P - 1) : 0;
+            s_pair[tid] = p;
+            s_row[tid] = a.x_per_pair ? p : p / a.Ktop;
+        }
+        int grow;
+        if (MODE == kModeUpSwiglu) grow = (ra < 64) ? rb * 64 + ra : a.Ru + rb * 64 + (ra - 64);
+        else grow = rb * 128 + ra;
+        const size_t wrow = (size_t)e * a.N + grow;
+        const uint32_t* wp = a.w + wrow * (size_t)(a.Kd / 16) + half * 2;
+        const uint16_t* sp = a.s + wrow * nsb;
+        const uint16_t* bp = a.b + wrow * nsb;
+        uint2 cw = *reinterpret_cast<const uint2*>(wp);
+        uint16_t cs = sp[0], cb = bp[0];
+        __syncthreads();  // s_row ready; the previous tile's epilogue is done with shared memory
+
+#pragma unroll 1
+        for (int kb = 0; kb < KB; ++kb) {
+            const int s = kb & 1;
+            if (pending[s]) wait_stage(s);  // the MMAs that read this stage two k-blocks ago
+            unsigned char* sA = smem + s * kStageBytes;  // hi
+            unsigned char* sL = sA + kStageA;             // lo
+            unsigned char* sB = sL + kStageA;
+            for (int i = tid; i < nmma * 8; i += kGroupedThreads) {
+                const int n = i >> 3, part = i & 7;
+                const bool v = n < cnt;
+                const uint16_t* src = a.x + (size_t)(v ? s_row[n] : 0) * a.Kd + kb * 64 + part * 8;
+                cp_async16(smem_u32(sB + sw128(n, part * 8)), src, v);
+            }
+            cp_async_commit();
+            {
+                const float sc = Half<DT>::to_f(cs), bi2 = Half<DT>::to_f(cb);
+                const uint32_t c2[2] = {cw.x, cw.y};
+                if (kb + 1 < KB) {  // the next k-block's codes, scale and bias are in flight meanwhile
+                    cw = *reinterpret_cast<const uint2*>(wp + (kb + 1) * 4);
+                    const int g1 = ((kb + 1) * 64) / GS;
+                    cs = sp[g1];
+                    cb = bp[g1];
+                }
+#pragma unroll
+                for (int word = 0; word < 2; ++word) {
+                    uint32_t hi[8], lo[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const float q0 = (float)((c2[word] >> (4 * i)) & 3u);
+                        const float q1 = (float)((c2[word] >> (4 * i + 2)) & 3u);
+                        const float w0 = fmaf(sc, q0, bi2), w1 = fmaf(sc, q1, bi2);
+                        hi[i] = pack2<DT>(w0, w1);
+                        lo[i] = pack2<DT>(w0 - Half<DT>::to_f((uint16_t)(hi[i] & 0xffffu)),
+                                          w1 - Half<DT>::to_f((uint16_t)(hi[i] >> 16)));
+                    }
+                    const int k0 = half * 32 + word * 16;
+                    const uint32_t o0 = sw128(ra, k0), o1 = sw128(ra, k0 + 8);
+                    *reinterpret_cast<uint4*>(sA + o0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                    *reinterpret_cast<uint4*>(sA + o1) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                    *reinterpret_cast<uint4*>(sL + o0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                    *reinterpret_cast<uint4*>(sL + o1) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                }
+            }
+            cp_async_wait<0>();
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
+            __syncthreads();
+            if (tid == 0) {
+                tc_fence_after();
+                const uint32_t idesc = idesc_f16<DT>(nmma);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t bd = sdesc_sw128(smem_u32(sB) + kk * 32);
+#pragma unroll
+                    for (int part = 0; part < 2; ++part) {  // D += A_hi B, then D += A_lo B
+                        const uint64_t ad = sdesc_sw128(smem_u32(part ? sL : sA) + kk * 32);
+                        const uint32_t accum = (kb > 0 || kk > 0 || part > 0) ? 1u : 0u;
+                        asm volatile(
+                            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                            " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+                            "l"(ad), "l"(bd), "r"(idesc), "r"(accum));
+                    }
+                }
+                asm volatile(
+                    "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                        smem_u32(&s_bar[s])));
+            }
+            pending[s] = true;
+        }
+        for (int s = 0; s < kStages; ++s)
+            if (pending[s]) wait_stage(s);
+        tc_fence_after();
+
+        // ---- epilogue: warp w reads TMEM lanes 32 (w & 3) + lane, columns
+        // 64 (w >> 2) + [0, 64)
+        const int r = 32 * (warp & 3) + lane;  // A row = TMEM lane
+        const int c0 = 64 * (warp >> 2);
+        if (MODE == kModeUpSwiglu) {
+            float* sG = reinterpret_cast<float*>(smem);  // [token][64] gate sums (stage 0 is free)
+            if (r >= 64) {
+#pragma unroll 1
+                for (int cc = 0; cc < 64; cc += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + c0 + cc, v);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) sG[(c0 + cc + j) * 64 + (r - 64)] = __uint_as_float(v[j]);
+                }
+            }
+            tc_fence_before();
+            __syncthreads();
+            if (r < 64) {
+#pragma unroll 1
+                for (int cc = 0; cc < 64; cc += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + c0 + cc, v);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int n = c0 + cc + j;
+                        if (n < cnt)
+                            a.out[(size_t)s_pair[n] * a.Ru + rb * 64 + r] =
+                                swiglu_staged<DT>(__uint_as_float(v[j]), sG[n * 64 + r], a.clamp);
+                    }
+                }
+            }
+        } else {
+#pragma unroll 1
+            for (int cc = 0; cc < 64; cc += 16) {
+                uint32_t v[16];
+                tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + c0 + cc, v);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int n = c0 + cc + j;
+                    if (n < cnt)
+                        a.out[(size_t)s_pair[n] * a.N + rb * 128 + r] = Half<DT>::from_f(__uint_as_float(v[j]));
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();  // TMEM reads done before the next tile's first MMA; shared memory free
+        tc_fence_after();
+    }
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    if (tid == 0 && s_timeout) atomicExch(a.status + 2, MOMIJ_ERR_TIMEOUT);
+    pdl_launch_dependents();
+}
+
+#define MOMIJ_GROUPED_INST(DT, GS)                                               \
+    template __global__ void grouped_gemm_kernel<DT, GS, kModeUpSwiglu>(const GroupedArgs); \
+    template __global__ void grouped_gemm_kernel<DT, GS, kModeRows>(const GroupedArgs);
+MOMIJ_GROUPED_INST(MOMIJ_DTYPE_BF16, 64)
+MOMIJ_GROUPED_INST(MOMIJ_DTYPE_BF16, 128)
+MOMIJ_GROUPED_INST(MOMIJ_DTYPE_F16, 64)
+MOMIJ_GROUPED_INST(MOMIJ_DTYPE_F16, 128)
+
+}  // namespace momij

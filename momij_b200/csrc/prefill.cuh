@@ -1,0 +1,48 @@
+// prefill.cuh -- the grouped (per-expert) GEMM path for prefill and large
+// verify batches: tokens are permuted by expert (permute_kernel), cut into
+// blocks of <= kBlockTokens sorted pairs of one expert, and every (block, 128
+// weight rows) tile runs on the 5th-generation tensor cores (tcgen05, fp32
+// accumulators in TMEM) with the 2-bit weights dequantised into bf16/f16
+// shared-memory tiles.
+#pragma once
+
+#include "kernels.cuh"
+
+namespace momij {
+
+constexpr int kBlockTokens = 128;  // MMA N (tokens) per tile, at most
+constexpr int kGroupedThreads = 256;
+
+// Block list header (int32): [0] blocks.  Entries from +4: (expert, first
+// sorted position, pairs, 0).
+constexpr int kBlockHeader = 4;
+__host__ __device__ constexpr size_t block_list_ints(int P, int E) {
+    return kBlockHeader + 4 * ((size_t)P / kBlockTokens + (size_t)E + 1);
+}
+
+struct GroupedArgs {
+    const uint16_t* x;       // activation rows [rows, Kd]
+    int x_per_pair;          // 1: row of pair p is p; 0: p / Ktop
+    const uint32_t* w;       // [E, N, Kd/16]
+    const uint16_t* s;       // [E, N, Kd/gs]
+    const uint16_t* b;
+    const int32_t* blocks;   // block list (see above)
+    const int32_t* pairs;    // sorted pair ids
+    int32_t* status;         // work-plan header: [1] routing status, [2] error word (both 0: run);
+                             // a stuck MMA wait records MOMIJ_ERR_TIMEOUT in [2]
+    uint16_t* out;           // up||gate mode: act [P, Ru]; rows mode: [P, N]
+    int Kd, N, Ru, Ktop;     // Ru: up||gate mode: first gate row (= I)
+    int E, P;                // experts, pairs (bounds of the block list entries)
+    float clamp;
+};
+
+// Builds the block list from the per-expert offsets of permute_kernel.
+__global__ void block_list_kernel(const int32_t* offsets, int E, int32_t* blocks,
+                                  const int32_t* status);
+
+// MODE kModeUpSwiglu: tile = 64 up rows + the matching 64 gate rows, output the
+// staged clamped SwiGLU; kModeRows: 128 output rows.
+template <int DT, int GS, int MODE>
+__global__ void grouped_gemm_kernel(const GroupedArgs a);
+
+}  // namespace momij

@@ -137,6 +137,7 @@ __global__ void __launch_bounds__(1024) permute_kernel(const int32_t* __restrict
     extern __shared__ int s_cnt[];  // E + 1
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     __shared__ int s_bad;
+    pdl_wait();  // the indices may come from the previous kernel on the stream
     if (threadIdx.x == 0) s_bad = 0;
     __syncthreads();
     for (int i = threadIdx.x; i < P; i += blockDim.x) {

@@ -29,7 +29,8 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "momij_moe.h")
 OK, UNSUPPORTED_SHAPE, NOT_READY, NO_DEVICE, INVALID_ARGUMENT = 0, 1, 2, 3, 4
 EXPERT_INDEX, WORKSPACE, CUDA, NCCL, TIMEOUT, STOPPED = 5, 6, 7, 8, 9, 10
 DTYPE_BF16, DTYPE_F16 = 0, 1
-MAX_PAIRS = 1024
+MAX_PAIRS = 1024          # gqmm2 surfaces (MOMIJ_MAX_PAIRS)
+MAX_GROUPED_PAIRS = 65536  # expert_ffn / forward through the grouped path
 
 
 class SeedlessError(RuntimeError):
