@@ -42,17 +42,20 @@ CONFIGS = {
     "verify": dict(desc="BASELINE config 2: verify batch M=8 (rho=0.7 correlated logits), "
                         "config-1 shapes, 48 layers", H=4096, I=1536, E=128, K=8, gs=64, M=8,
                    L=48, rho=0.7),
+    "prefill": dict(desc="BASELINE config 3: prefill of 2048 tokens through one MoE layer, "
+                         "Zipf(1.1) routing, grouped tcgen05 GEMM path", H=4096, I=1536, E=128,
+                    K=8, gs=64, M=2048, L=1, rho=None, zipf=1.1),
 }
 METRIC = "2-bit MoE gather-GEMV tokens/s"
 
 
-def load_peaks() -> tuple[float, str]:
+def load_peaks(key: str = "hbm_gbs") -> tuple[float, str]:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(p) as f:
-            return float(json.load(f)["hbm_gbs"]), "measured"
+            return float(json.load(f)[key]), "measured"
     except Exception:
-        return 6650.0, "fallback"
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}.get(key, 0.0), "fallback"
 
 
 class ClockSampler:
@@ -153,6 +156,8 @@ def cpu_layer_sample(cfg: dict, wh: dict, x: np.ndarray, inds: np.ndarray, score
     """Times oracle.expert_ffn on one layer's selected experts for ~budget_s."""
     from oracle import oracle as O
     M, H, I, K, gs = cfg["M"], cfg["H"], cfg["I"], cfg["K"], cfg["gs"]
+    if M > 64:  # large batches: a bounded sample of the tokens, scaled per token
+        M, x, inds, scores = 64, x[:64], inds[:64], scores[:64]
     O.expert_ffn(x, wh, inds, scores, M, H, I, K, gs)  # warm
     n, t0 = 0, time.perf_counter()
     while True:
@@ -163,10 +168,19 @@ def cpu_layer_sample(cfg: dict, wh: dict, x: np.ndarray, inds: np.ndarray, score
     dt = (time.perf_counter() - t0) / n
     tok_s = M / (dt * cfg["L"])
     return {"value": tok_s, "unit": "tokens/s", "cores": O.num_threads(), "kind": "port",
-            "sample": f"{n} evaluations of one layer's expert FFN ({cfg['M']} token(s), "
+            "sample": f"{n} evaluations of one layer's expert FFN ({M} token(s), "
                       f"{len(np.unique(inds))} experts, {dt * 1e3:.1f} ms each); tokens/s scaled to "
                       f"{cfg['L']} layers",
             "layer_ms": dt * 1e3}
+
+
+def cfg_logits(S, cfg: dict, layer: int) -> np.ndarray:
+    M, E = cfg["M"], cfg["E"]
+    if cfg.get("zipf"):
+        return S.logits_zipf(M, E, cfg["zipf"], layer, 0)
+    if cfg["rho"]:
+        return S.logits_ar1(M, E, cfg["rho"], layer, 0)
+    return S.logits_normal(M, E, layer, 0)
 
 
 def host_layer_inputs(cfg: dict, layer: int = 0):
@@ -174,8 +188,7 @@ def host_layer_inputs(cfg: dict, layer: int = 0):
     import torch
     from momij_b200 import moe, synth as S
     H, I, E, K, gs, M = (cfg[k] for k in ("H", "I", "E", "K", "gs", "M"))
-    lg = (S.logits_ar1(M, E, cfg["rho"], layer, 0) if cfg["rho"]
-          else S.logits_normal(M, E, layer, 0))
+    lg = cfg_logits(S, cfg, layer)
     from oracle import oracle as O
     inds, scores = O.route(lg, K)
     uniq, remap = np.unique(inds, return_inverse=True)
@@ -196,7 +209,7 @@ def run_reference(args, cfg) -> None:
     from oracle import oracle as O
     H, I, E, K, gs, M = (cfg[k] for k in ("H", "I", "E", "K", "gs", "M"))
     # The CPU leg needs no GPU: generate the selected experts' weights on the host.
-    lg = (S.logits_ar1(M, E, cfg["rho"], 0, 0) if cfg["rho"] else S.logits_normal(M, E, 0, 0))
+    lg = cfg_logits(S, cfg, 0)
     inds, scores = O.route(lg, K)
     uniq, remap = np.unique(inds, return_inverse=True)
     full = {}
@@ -212,6 +225,8 @@ def run_reference(args, cfg) -> None:
                             .reshape(shape) for e in uniq])
     x = S.activations(M, H, 0, 0)
     rinds = remap.reshape(M, K).astype(np.int32)
+    if M > 64:  # large batches: each step is a bounded sample of 64 tokens, scaled per token
+        M, x, rinds, scores = 64, x[:64], rinds[:64], scores[:64]
     for _ in range(args.warmup):
         O.expert_ffn(x, full, rinds, scores, M, H, I, K, gs)
     t0 = time.perf_counter()
@@ -251,8 +266,7 @@ def run_gpu(args, cfg) -> None:
     P = M * K
     dev = torch.device("cuda", local)
     W = [moe.device_expert_weights(E, H, I, gs, layer=l, seed=0, device=dev) for l in range(L)]
-    lg_host = np.stack([(S.logits_ar1(M, E, cfg["rho"], l, 0) if cfg["rho"]
-                         else S.logits_normal(M, E, l, 0)) for l in range(L)])
+    lg_host = np.stack([cfg_logits(S, cfg, l) for l in range(L)])
     x_host = S.activations(M, H, 0, 0)
     logits = torch.from_numpy(lg_host).to(dev)
     h0 = torch.from_numpy(x_host.view(np.int16)).to(dev).view(torch.bfloat16)
@@ -367,6 +381,20 @@ def run_gpu(args, cfg) -> None:
     avg = {kid: (kt[kid][0] / kt[kid][1] if kt[kid][1] else None) for kid in kt}
     launches_per_layer = sum(1 for kid in kids if kt[kid][1]) or 1
     peak, peak_kind = load_peaks()
+    tensor_roof = None
+    if cfg.get("zipf"):
+        # grouped tcgen05 path: tensor-bound; the up||gate GEMM dominates
+        tpeak, tpeak_kind = load_peaks("bf16_tflops")
+        flops = 2.0 * P * (2 * I) * H  # algorithmic (the hi/lo split issues twice this)
+        t_ms = avg[moe.KERNEL_UP]
+        ach = flops / (t_ms * 1e-3) / 1e12 if t_ms else None
+        tensor_roof = {"bound": "tensor", "kernel": "grouped_gemm_kernel<up||gate+SwiGLU> (tcgen05)",
+                       "achieved": ach, "peak": tpeak, "unit": "TFLOP/s",
+                       "frac": (ach / tpeak) if ach else None, "traffic": None,
+                       "peak_source": tpeak_kind, "flops_per_launch": flops,
+                       "avg_launch_us": {"permute+blocks": _us(avg[moe.KERNEL_PLAN]),
+                                         "up": _us(avg[moe.KERNEL_UP]), "down": _us(avg[moe.KERNEL_ROWS]),
+                                         "combine": _us(avg[moe.KERNEL_COMBINE])}}
     if avg[moe.KERNEL_LAYER]:
         # the whole layer is one kernel: all of the layer's distinct expert bytes
         dom_kernel = "moe_layer_kernel (route + up||gate/SwiGLU + down + combine)"
@@ -395,7 +423,8 @@ def run_gpu(args, cfg) -> None:
             "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "u8xs8->s32 tensor-core dot, f32 epilogue, bf16 I/O",
+            "dtype": ("bf16 tcgen05 GEMM (weights as hi+lo bf16), f32 accumulate, bf16 I/O"
+                      if cfg.get("zipf") else "u8xs8->s32 tensor-core dot, f32 epilogue, bf16 I/O"),
             "data": "synthetic (seeded generator, momij_b200/synth.py)",
             "config": {"workload": cfg["desc"], "H": H, "E": E, "top_k": K, "I": I, "gs": gs,
                        "M": M, "layers": L, "global_batch": M * world,
@@ -404,7 +433,7 @@ def run_gpu(args, cfg) -> None:
                              "expert weights streamed per step"},
             "hbm_tbs": bytes_per_step / (ms_per_step * 1e-3) / 1e12,
             "hbm_frac_of_peak": bytes_per_step / (ms_per_step * 1e-3) / 1e9 / peak,
-            "roofline": {"bound": "hbm", "kernel": dom_kernel,
+            "roofline": tensor_roof if tensor_roof else {"bound": "hbm", "kernel": dom_kernel,
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": (achieved / peak) if achieved else None, "traffic": traffic,
                          "peak_source": peak_kind,

@@ -599,7 +599,7 @@ int run_grouped(const void* x, const uint32_t* w_ug, const void* s_ug, const voi
     if (rc) return rc;
     const int G = current_device_sm_count();
     if (G <= 0) return MOMIJ_ERR_CUDA;
-    const size_t smem = 2 * (2 * 128 * 128 + kBlockTokens * 128) + 1024;  // 2 stages x (A hi, A lo, B)
+    const size_t smem = 3 * (2 * 128 * 128 + kBlockTokens * 128) + 1024;  // 3 stages x (A hi, A lo, B)
     for (int mode : {kModeUpSwiglu, kModeRows}) {
         GroupedArgs a{};
         a.x = static_cast<const uint16_t*>(mode == kModeUpSwiglu ? x : ws.act);

@@ -32,7 +32,7 @@ namespace {
 constexpr int kStageA = 128 * 128;           // 128 weight rows x 64 elements x 2 B (one of hi / lo)
 constexpr int kStageB = kBlockTokens * 128;  // tokens x 64 elements x 2 B
 constexpr int kStageBytes = 2 * kStageA + kStageB;
-constexpr int kStages = 2;
+constexpr int kStages = 3;  // k-block stages: B of k-block kb+1 loads while kb is dequantised and kb-1 multiplies
 constexpr int kTmemCols = kBlockTokens;      // fp32 accumulator columns
 constexpr int kMmaWaitLimit = 1 << 24;
 
@@ -153,8 +153,8 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
     tc_fence_after();
     const uint32_t tmem = s_tmem;
 
-    uint32_t phase[kStages] = {0u, 0u};
-    bool pending[kStages] = {false, false};
+    uint32_t phase[kStages] = {0u, 0u, 0u};
+    bool pending[kStages] = {false, false, false};
     auto wait_stage = [&](int s) {
         bool ok = false;
         for (int it = 0; it < kMmaWaitLimit && !ok; ++it) ok = mbar_try_wait(&s_bar[s], phase[s]);
@@ -195,20 +195,31 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
         uint16_t cs = sp[0], cb = bp[0];
         __syncthreads();  // s_row ready; the previous tile's epilogue is done with shared memory
 
-#pragma unroll 1
-        for (int kb = 0; kb < KB; ++kb) {
-            const int s = kb & 1;
-            if (pending[s]) wait_stage(s);  // the MMAs that read this stage two k-blocks ago
-            unsigned char* sA = smem + s * kStageBytes;  // hi
-            unsigned char* sL = sA + kStageA;             // lo
-            unsigned char* sB = sL + kStageA;
+        // token rows of k-block kb into stage st (its previous MMAs are done)
+        auto issue_b = [&](int kb, int st) {
+            unsigned char* sB = smem + st * kStageBytes + 2 * kStageA;
             for (int i = tid; i < nmma * 8; i += kGroupedThreads) {
                 const int n = i >> 3, part = i & 7;
                 const bool v = n < cnt;
                 const uint16_t* src = a.x + (size_t)(v ? s_row[n] : 0) * a.Kd + kb * 64 + part * 8;
                 cp_async16(smem_u32(sB + sw128(n, part * 8)), src, v);
             }
-            cp_async_commit();
+        };
+        issue_b(0, 0);
+        cp_async_commit();
+
+#pragma unroll 1
+        for (int kb = 0; kb < KB; ++kb) {
+            const int s = kb % kStages;
+            if (kb + 1 < KB) {  // next k-block's token rows into the stage of k-block kb - 2
+                const int sn = (kb + 1) % kStages;
+                if (pending[sn]) wait_stage(sn);
+                issue_b(kb + 1, sn);
+            }
+            cp_async_commit();  // one group per k-block (possibly empty)
+            unsigned char* sA = smem + s * kStageBytes;  // hi
+            unsigned char* sL = sA + kStageA;             // lo
+            unsigned char* sB = sL + kStageA;
             {
                 const float sc = Half<DT>::to_f(cs), bi2 = Half<DT>::to_f(cb);
                 const uint32_t c2[2] = {cw.x, cw.y};
@@ -238,7 +249,7 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
                     *reinterpret_cast<uint4*>(sL + o1) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
                 }
             }
-            cp_async_wait<0>();
+            cp_async_wait<1>();  // this k-block's token rows (the next k-block's may be in flight)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
             __syncthreads();
             if (tid == 0) {
