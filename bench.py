@@ -45,6 +45,11 @@ CONFIGS = {
     "prefill": dict(desc="BASELINE config 3: prefill of 2048 tokens through one MoE layer, "
                          "Zipf(1.1) routing, grouped tcgen05 GEMM path", H=4096, I=1536, E=128,
                     K=8, gs=64, M=2048, L=1, rho=None, zipf=1.1),
+    "ep": dict(desc="BASELINE config 4: expert-parallel decode, 64 concurrent sequences (M=64 per "
+                    "step), H=4096, E=256, top-8, I=1024, gs64, 48 layers, N(0,1) router logits "
+                    "(uniform expert choice); experts sharded evenly over the GPUs, all-to-all "
+                    "dispatch/combine over NCCL", H=4096, I=1024, E=256, K=8, gs=64, M=64, L=48,
+               rho=None, ep=True),
 }
 METRIC = "2-bit MoE gather-GEMV tokens/s"
 
@@ -456,6 +461,191 @@ def run_gpu(args, cfg) -> None:
         dist.destroy_process_group()
 
 
+def run_ep(args, cfg) -> None:
+    """Config 4: M tokens per step split evenly over the ranks (each rank owns
+    M/N sequences and E/N experts); per layer route -> dispatch -> all-to-all
+    -> local experts -> all-to-all -> combine (momij_b200/ep.py).  Strong
+    scaling: the total work per step is fixed as N grows.  On one GPU the
+    step is the plain single-GPU layer (moe.forward), the best one-GPU path."""
+    import torch
+    world, rank, local = dist_setup()
+    torch.cuda.set_device(local)
+    from momij_b200 import moe, synth as S
+    from momij_b200.ep import ExpertParallelMoE, GpuOps
+
+    H, I, E, K, gs, M, L = (cfg[k] for k in ("H", "I", "E", "K", "gs", "M", "L"))
+    if M % world or E % world:
+        raise SystemExit(f"ep config needs N dividing M={M} and E={E}")
+    Ml, El = M // world, E // world
+    lo = rank * El
+    dev = torch.device("cuda", local)
+    W = [moe.device_expert_weights(E, H, I, gs, layer=l, seed=0, device=dev, experts=(lo, lo + El))
+         for l in range(L)]
+    mine = slice(rank * Ml, (rank + 1) * Ml)
+    lg_host = np.ascontiguousarray(np.stack([cfg_logits(S, cfg, l)[mine] for l in range(L)]))
+    x_host = np.ascontiguousarray(S.activations(M, H, 0, 0)[mine])
+    logits = torch.from_numpy(lg_host).to(dev)
+    h = torch.from_numpy(x_host.view(np.int16)).to(dev).view(torch.bfloat16)
+    stream = torch.cuda.Stream(device=dev)
+    ops = GpuOps(W[0], H=H, I=I, gs=gs, stream=stream)
+    layer = ExpertParallelMoE(ops, E=E, H=H, I=I, K=K, M=Ml, device=dev)
+    ws = moe.new_workspace(Ml, K, H, I, dev)
+    inds_all = torch.empty(L, Ml, K, dtype=torch.int32, device=dev)
+    scores_all = torch.empty(L, Ml, K, dtype=torch.float32, device=dev)
+
+    def step():
+        for l in range(L):
+            if world == 1:
+                moe.forward(logits[l], h, W[l], None, H=H, I=I, Ktop=K, gs=gs, M=Ml, inds=inds_all[l],
+                            scores=scores_all[l], resid_h=h, workspace=ws, stream=stream)
+            else:
+                ops.w = W[l]
+                layer.inds, layer.scores = inds_all[l], scores_all[l]
+                layer.forward(logits[l], h)
+
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    if int(layer.status.item()) != 0:
+        raise SystemExit(f"ep status {int(layer.status.item())}")
+    # algorithmic bytes of this rank: its experts that the step's tokens select
+    ih = inds_all.cpu().numpy()
+    if world > 1:  # every rank's routing, to count the local experts used
+        import torch.distributed as dist
+        g = [torch.empty_like(inds_all) for _ in range(world)]
+        dist.all_gather(g, inds_all)
+        ih = np.concatenate([t.cpu().numpy() for t in g], axis=1)
+    eb = S.expert_bytes(H, I, gs)
+    used = [int(((np.unique(ih[l]) >= lo) & (np.unique(ih[l]) < lo + El)).sum()) for l in range(L)]
+    bytes_per_step = sum(used) * eb
+
+    graph = None
+    if os.environ.get("MOMIJ_EP_GRAPH", "1") != "0":
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step()
+            torch.cuda.synchronize()
+        except Exception as e:  # eager fallback keeps the same collectives on every rank
+            print(f"warning: graph capture failed ({e}); timing eager launches", file=sys.stderr)
+            graph = None
+            torch.cuda.synchronize()
+    ok = torch.tensor([1 if graph is not None else 0], device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    if not int(ok.item()):
+        graph = None
+
+    def run():
+        with torch.cuda.stream(stream):
+            if graph is not None:
+                graph.replay()
+            else:
+                step()
+
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        barrier(world)
+        ev0.record(stream)
+        for _ in range(args.steps):
+            run()
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    dev_ms = max_over_ranks(ev0.elapsed_time(ev1), world)
+    clocks = clk.summary()
+    ms_per_step = dev_ms / args.steps
+    tok_s = M * args.steps / (dev_ms / 1e3)
+
+    x_pin = torch.from_numpy(x_host.view(np.int16)).view(torch.bfloat16).pin_memory()
+    lg_pin = torch.from_numpy(lg_host).pin_memory()
+    y_pin = torch.empty(Ml, H, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            h.copy_(x_pin, non_blocking=True)
+            logits.copy_(lg_pin, non_blocking=True)
+        run()
+        with torch.cuda.stream(stream):
+            y_pin.copy_(h, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    e2e_tok_s = M * args.steps / (e2e_ms / 1e3)
+
+    # per-kernel durations from one instrumented eager step
+    moe.profile_reset()
+    moe.profile_enable(True)
+    with torch.cuda.stream(stream):
+        step()
+    torch.cuda.synchronize()
+    moe.profile_enable(False)
+    kids = (moe.KERNEL_PLAN, moe.KERNEL_UP, moe.KERNEL_ROWS, moe.KERNEL_COMBINE, moe.KERNEL_LAYER)
+    kt = {kid: moe.profile_read(kid) for kid in kids}
+    moe.profile_reset()
+    launches = sum(n for _, n in kt.values())
+    up_ms = kt[moe.KERNEL_UP][0] / max(kt[moe.KERNEL_UP][1], 1)
+    dn_ms = kt[moe.KERNEL_ROWS][0] / max(kt[moe.KERNEL_ROWS][1], 1)
+    up_b = (2 * I) * (H // 16) * 4 + (2 * I) * (H // gs) * 4
+    up_bytes = sum(used) / L * up_b
+    achieved = up_bytes / (up_ms * 1e-3) / 1e9 if kt[moe.KERNEL_UP][1] else None
+    peak, peak_kind = load_peaks()
+    if world > 1:  # dispatch + combine gathers/kernels beside the instrumented ones
+        launches += 3 * L
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        wh, xh, ihh, sh = host_layer_inputs(cfg, 0)
+        cpu = cpu_layer_sample(cfg, wh, xh, ihh, sh, args.cpu_seconds)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "u8xs8->s32 tensor-core dot, f32 epilogue, bf16 I/O",
+            "data": "synthetic (seeded generator, momij_b200/synth.py)",
+            "config": {"workload": cfg["desc"], "H": H, "E": E, "top_k": K, "I": I, "gs": gs,
+                       "M": M, "layers": L, "global_batch": M, "tokens_per_rank": Ml,
+                       "experts_per_rank": El,
+                       "parallelism": f"ep{world}" if world > 1 else "single",
+                       "graph": graph is not None,
+                       "l2": f"inputs larger than L2: {bytes_per_step / 1e9:.2f} GB of distinct "
+                             "expert weights streamed per step on rank 0"},
+            "hbm_tbs_rank0": bytes_per_step / (ms_per_step * 1e-3) / 1e12,
+            "roofline": {"bound": "hbm", "kernel": "gemv_kernel<up||gate+SwiGLU>",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": (achieved / peak) if achieved else None, "traffic": None,
+                         "peak_source": peak_kind, "bytes_per_launch": up_bytes,
+                         "avg_launch_us": {"up": _us(up_ms), "down": _us(dn_ms)}},
+            "clocks": clocks,
+            "e2e": {"value": e2e_tok_s, "unit": "tokens/s", "h2d_bytes_per_step": x_pin.numel() * 2
+                    + lg_pin.numel() * 4, "d2h_bytes_per_step": y_pin.numel() * 2,
+                    "ms_per_step": e2e_ms / args.steps},
+            "gpu_launches": launches * args.steps,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def _us(ms):
     return None if ms is None else ms * 1e3
 
@@ -480,6 +670,8 @@ def main() -> None:
         cfg["desc"] += f" [profiling case: {args.layers} layers]"
     if args.impl == "reference":
         run_reference(args, cfg)
+    elif cfg.get("ep"):
+        run_ep(args, cfg)
     else:
         run_gpu(args, cfg)
 

@@ -99,6 +99,8 @@ size_t momij_moe_workspace_size(int M, int Ktop, int H, int I);
  * with e = inds[mk], mk in [0, M*Ktop), row = mk if lhs_per_expert else
  * mk / Ktop.  x [M or M*Ktop, Kdim], out [M*Ktop, N].  Each distinct expert's
  * rows are streamed once per call (tokens sharing an expert share the load).
+ * inds[mk] == -1 marks an empty slot (expert-parallel receive buffers): its
+ * output row is left untouched.  Same for momij_moe_gqmm2_up_swiglu.
  * Replaces: SeedlessMetal.gqmm2 (SeedlessMetal.swift:312-438, kernel
  * gqmm2_rows :2168-2221) and MLX.gatherQuantizedMM(transpose:true, bits:2,
  * mode:.affine) (MapleMoE.swift:65-75). */
@@ -178,6 +180,35 @@ int momij_moe_forward(const float* logits, const void* x, const uint32_t* w_ug, 
                       int32_t* inds, float* scores, void* y, void* resid_h, int M, int H, int I,
                       int E, int Ktop, int gs, float clamp, int dtype, void* workspace,
                       size_t workspace_bytes, momij_stream_t stream);
+
+/* Expert-parallel decode (experts sharded contiguously: rank r owns experts
+ * [r*E/world, (r+1)*E/world)).  The caller runs the two all-to-all exchanges
+ * with its own NCCL communicator (ncclSend/ncclRecv or all-to-all of equal
+ * splits of `capacity` rows per rank):
+ *   1. momij_moe_ep_dispatch: pair p = m*K + k of this rank's M tokens goes to
+ *      rank dest = inds[p] / (E/world) at row slot_map[p] = dest*capacity +
+ *      (its rank among the pairs bound for dest, in pair order) of send_x
+ *      [world*capacity, H] (the token's row x[m]) and send_meta
+ *      [world*capacity] (the expert's local index; -1 marks empty rows).
+ *      capacity >= M*K.  *status (device int32): MOMIJ_OK or
+ *      MOMIJ_ERR_EXPERT_INDEX.
+ *   2. all-to-all(send_x -> recv_x), all-to-all(send_meta -> recv_meta);
+ *   3. momij_moe_gqmm2_up_swiglu(recv_x, ..., recv_meta, act, M=world*capacity,
+ *      Ktop=1) and momij_moe_gqmm2(act, ..., recv_meta, down, M=world*capacity,
+ *      Ktop=1) with the rank's local experts (empty rows are skipped);
+ *   4. all-to-all(down -> back);
+ *   5. momij_moe_ep_combine: y[m] = sum_k scores[m,k] * back[slot_map[m*K+k]]
+ *      in fp32 in k order, rounded once, or added into resid_h like
+ *      momij_moe_score_resid -- the same bits as the single-GPU combine.
+ * Replaces: no counterpart in the reference (it runs on one GPU); the expert
+ * split follows north-star config 4 (experts sharded evenly, all-to-all
+ * dispatch and combine over NVLink). */
+int momij_moe_ep_dispatch(const int32_t* inds, const void* x, int M, int K, int E, int world,
+                          int capacity, int H, void* send_x, int32_t* send_meta, int32_t* slot_map,
+                          int32_t* status, momij_stream_t stream);
+int momij_moe_ep_combine(const void* back, const float* scores, const int32_t* slot_map, void* y,
+                         void* resid_h, int M, int K, int H, int dtype, const int32_t* status,
+                         momij_stream_t stream);
 
 /* Per-kernel GPU timing.  While enabled, each launch made by the entry points
  * above is bracketed by two CUDA events on its stream (also when the stream

@@ -512,10 +512,11 @@ int tmax_for(int M, int Ktop, int lhs_per_expert) {
     (void)Ktop;
 }
 
-int launch_plan(const int32_t* inds, int P, int E, int tmax, int32_t* plan, cudaStream_t st) {
+int launch_plan(const int32_t* inds, int P, int E, int tmax, int32_t* plan, cudaStream_t st,
+                int allow_pad = 0) {
     const int slot = prof_begin(MOMIJ_KERNEL_PLAN, st);
-    const int rc =
-        cuda_status(launch(plan_kernel, dim3(1), dim3(1024), 0, st, inds, P, E, tmax, plan));
+    const int rc = cuda_status(
+        launch(plan_kernel, dim3(1), dim3(1024), 0, st, inds, P, E, tmax, plan, allow_pad));
     prof_end(slot, st);
     return rc;
 }
@@ -780,7 +781,7 @@ int momij_moe_gqmm2(const void* x, const uint32_t* w, const void* scales, const 
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     int32_t* plan = static_cast<int32_t*>(workspace);
     const int tmax = tmax_for(M, Ktop, lhs_per_expert);
-    int rc = launch_plan(inds, M * Ktop, E, tmax, plan, st);
+    int rc = launch_plan(inds, M * Ktop, E, tmax, plan, st, /*allow_pad=*/1);
     if (rc) return rc;
     GemvLaunch L = make_launch(x, lhs_per_expert ? 1 : 0, w, scales, biases, plan, out, Kdim, N, E,
                                M, Ktop, N, N, 0.f);
@@ -807,7 +808,7 @@ int momij_moe_gqmm2_up_swiglu(const void* x, const uint32_t* w, const void* scal
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     int32_t* plan = static_cast<int32_t*>(workspace);
     const int tmax = tmax_for(M, Ktop, 0);
-    int rc = launch_plan(inds, M * Ktop, E, tmax, plan, st);
+    int rc = launch_plan(inds, M * Ktop, E, tmax, plan, st, /*allow_pad=*/1);
     if (rc) return rc;
     GemvLaunch L = make_launch(x, 0, w, scales, biases, plan, act, H, 2 * I, E, M, Ktop, I, I, clamp);
     return run_gemv(L, kModeUpSwiglu, tmax, dtype, gs, st);
@@ -942,6 +943,55 @@ int momij_moe_forward(const float* logits, const void* x, const uint32_t* w_ug, 
     if (rc) return rc;
     return ffn_after_plan(x, w_ug, s_ug, b_ug, w_dn, s_dn, b_dn, sc_out, y, resid_h, M, H, I, E,
                           Ktop, gs, clamp, dtype, tmax, ws, st);
+}
+
+int momij_moe_ep_dispatch(const int32_t* inds, const void* x, int M, int K, int E, int world,
+                          int capacity, int H, void* send_x, int32_t* send_meta, int32_t* slot_map,
+                          int32_t* status, momij_stream_t stream) {
+    if (int rc = check_device()) return rc;
+    if (M < 0 || K < 1 || E < 1 || world < 1 || capacity < 0 || H < 8) return MOMIJ_ERR_INVALID_ARGUMENT;
+    if (E % world || (long long)M * K > MOMIJ_MAX_PAIRS || (long long)M * K > capacity || H % 8)
+        return MOMIJ_ERR_UNSUPPORTED_SHAPE;
+    if (M == 0) return MOMIJ_OK;
+    if (!inds || !x || !send_x || !send_meta || !slot_map || !status || !aligned(x, 16) ||
+        !aligned(send_x, 16))
+        return MOMIJ_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int P = M * K;
+    if (cudaMemsetAsync(status, 0, sizeof(int32_t), st) != cudaSuccess) return MOMIJ_ERR_CUDA;
+    int rc = cuda_status(launch(ep_slots_kernel, dim3(1), dim3(1024), 0, st, inds, P, E, world, capacity,
+                                send_meta, slot_map, status));
+    if (rc) return rc;
+    const int row16 = H / 8;
+    const int blocks = (int)std::min<long long>(((long long)P * row16 + 255) / 256, 2048);
+    return cuda_status(launch(ep_gather_kernel, dim3(blocks), dim3(256), 0, st,
+                              static_cast<const uint4*>(x), static_cast<const int32_t*>(slot_map), P, K,
+                              row16, static_cast<uint4*>(send_x)));
+}
+
+int momij_moe_ep_combine(const void* back, const float* scores, const int32_t* slot_map, void* y,
+                         void* resid_h, int M, int K, int H, int dtype, const int32_t* status,
+                         momij_stream_t stream) {
+    if (int rc = check_device()) return rc;
+    if (M < 0 || K < 1 || H < 1 || (dtype != MOMIJ_DTYPE_BF16 && dtype != MOMIJ_DTYPE_F16))
+        return MOMIJ_ERR_INVALID_ARGUMENT;
+    if (M == 0) return MOMIJ_OK;
+    if (!back || !scores || !slot_map || !status || (!y && !resid_h)) return MOMIJ_ERR_INVALID_ARGUMENT;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const long long n = (long long)M * H;
+    const int blocks = (int)std::min<long long>((n + 255) / 256, 4096);
+    auto b = static_cast<const uint16_t*>(back);
+    auto o = static_cast<uint16_t*>(resid_h ? resid_h : y);
+    const bool r = resid_h != nullptr;
+    if (dtype == MOMIJ_DTYPE_BF16)
+        return cuda_status(r ? launch(ep_combine_kernel<MOMIJ_DTYPE_BF16, 1>, dim3(blocks), dim3(256), 0, st, b,
+                                      scores, slot_map, o, M, K, H, status)
+                             : launch(ep_combine_kernel<MOMIJ_DTYPE_BF16, 0>, dim3(blocks), dim3(256), 0, st, b,
+                                      scores, slot_map, o, M, K, H, status));
+    return cuda_status(r ? launch(ep_combine_kernel<MOMIJ_DTYPE_F16, 1>, dim3(blocks), dim3(256), 0, st, b,
+                                  scores, slot_map, o, M, K, H, status)
+                         : launch(ep_combine_kernel<MOMIJ_DTYPE_F16, 0>, dim3(blocks), dim3(256), 0, st, b,
+                                  scores, slot_map, o, M, K, H, status));
 }
 
 int momij_synth_fill(void* dst, int64_t n, int kind, float a, float c, uint64_t seed,

@@ -30,7 +30,7 @@ struct GemvArgs {
 
 __global__ void route_kernel(const float* logits, int M, int E, int K, int32_t* inds,
                              float* scores);
-__global__ void plan_kernel(const int32_t* inds, int P, int E, int tmax, int32_t* plan);
+__global__ void plan_kernel(const int32_t* inds, int P, int E, int tmax, int32_t* plan, int allow_pad);
 __global__ void route_plan_kernel(const float* logits, int M, int E, int K, int tmax,
                                   int32_t* inds, float* scores, int32_t* plan);
 __global__ void permute_kernel(const int32_t* inds, const float* scores, int P, int E,
@@ -44,6 +44,14 @@ __global__ void swiglu_kernel(const uint16_t* ug, uint16_t* act, int rows, int I
 template <int DT, int RESID>
 __global__ void combine_kernel(const uint16_t* down, const float* scores, uint16_t* y, int M,
                                int Ktop, int H, const int32_t* plan);
+// expert-parallel dispatch / combine (ep.cu)
+__global__ void ep_slots_kernel(const int32_t* inds, int P, int E, int world, int capacity,
+                                int32_t* send_meta, int32_t* slot_map, int32_t* status);
+__global__ void ep_gather_kernel(const uint4* x, const int32_t* slot_map, int P, int K, int row16,
+                                 uint4* send_x);
+template <int DT, int RESID>
+__global__ void ep_combine_kernel(const uint16_t* back, const float* scores, const int32_t* slot_map,
+                                  uint16_t* y, int M, int K, int H, const int32_t* status);
 __global__ void synth_fill_kernel(void* dst, int64_t n, int kind, float a, float c, uint64_t seed,
                                   uint64_t stream_id, int64_t start, int dtype);
 

@@ -25,9 +25,11 @@ __global__ void route_kernel(const float* __restrict__ logits, int M, int E, int
 //   (reset here), [3] reserved,
 //   [4 + 4u .. 4 + 4u + 3] unit u = (expert, first sorted position, count, 0),
 //   [4 + 4P + q] pair index at sorted position q.
-// Runs as one block of 1024 threads; P <= MOMIJ_MAX_PAIRS.
+// Runs as one block of 1024 threads; P <= MOMIJ_MAX_PAIRS.  allow_pad: an
+// index of -1 marks an empty slot (expert-parallel receive buffers): it joins
+// no unit, so its output row is left untouched.
 __device__ void build_plan_block(const int32_t* __restrict__ inds, int P, int E, int tmax,
-                                 int32_t* __restrict__ plan) {
+                                 int32_t* __restrict__ plan, int allow_pad) {
     __shared__ int s_e[MOMIJ_MAX_PAIRS];
     __shared__ int s_flag[MOMIJ_MAX_PAIRS];
     __shared__ int s_warp[32];
@@ -37,7 +39,7 @@ __device__ void build_plan_block(const int32_t* __restrict__ inds, int P, int E,
     __syncthreads();
     for (int i = tid; i < P; i += nt) {
         int e = inds[i];
-        if (e < 0 || e >= E) s_bad = 1;
+        if (e < (allow_pad ? -1 : 0) || e >= E) s_bad = 1;
         s_e[i] = e;
     }
     __syncthreads();
@@ -58,7 +60,7 @@ __device__ void build_plan_block(const int32_t* __restrict__ inds, int P, int E,
             my_before += (ej == my_e) & (j < tid);
         }
         my_pos = my_less + my_before;
-        s_flag[my_pos] = (my_before % tmax) == 0;
+        s_flag[my_pos] = my_e >= 0 && (my_before % tmax) == 0;  // empty slots sort first, no unit
         sorted[my_pos] = tid;
     }
     __syncthreads();
@@ -88,7 +90,7 @@ __device__ void build_plan_block(const int32_t* __restrict__ inds, int P, int E,
     // publish uid per sorted position back through s_flag
     if (tid < P) s_flag[tid] = f ? excl : -1;
     __syncthreads();
-    if (tid < P && (my_before % tmax) == 0) {
+    if (tid < P && my_e >= 0 && (my_before % tmax) == 0) {
         int u = s_flag[my_pos];
         int cnt = my_cnt - my_before;
         units[4 * u + 0] = my_e;
@@ -104,9 +106,10 @@ __device__ void build_plan_block(const int32_t* __restrict__ inds, int P, int E,
 }
 
 __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ inds, int P,
-                                                    int E, int tmax, int32_t* __restrict__ plan) {
+                                                    int E, int tmax, int32_t* __restrict__ plan,
+                                                    int allow_pad) {
     pdl_wait();
-    build_plan_block(inds, P, E, tmax, plan);
+    build_plan_block(inds, P, E, tmax, plan, allow_pad);
     pdl_launch_dependents();
 }
 
@@ -121,7 +124,7 @@ __global__ void __launch_bounds__(1024) route_plan_kernel(const float* __restric
     for (int m = threadIdx.x >> 5; m < M; m += warps)
         route_token_warp(logits + (size_t)m * E, E, K, inds + (size_t)m * K, scores + (size_t)m * K);
     __syncthreads();
-    build_plan_block(inds, M * K, E, tmax, plan);
+    build_plan_block(inds, M * K, E, tmax, plan, 0);
     pdl_launch_dependents();
 }
 

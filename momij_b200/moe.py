@@ -64,6 +64,8 @@ def _load() -> ctypes.CDLL:
     L.momij_moe_score_resid.argtypes = [vp, vp, vp, i, i, i, i, vp]
     L.momij_moe_expert_ffn.argtypes = [vp] * 11 + [i] * 6 + [f, i, vp, sz, vp]
     L.momij_moe_forward.argtypes = [vp] * 12 + [i] * 6 + [f, i, vp, sz, vp]
+    L.momij_moe_ep_dispatch.argtypes = [vp, vp] + [i] * 6 + [vp, vp, vp, vp, vp]
+    L.momij_moe_ep_combine.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, vp, vp]
     L.momij_synth_fill.argtypes = [vp, ctypes.c_int64, i, f, f, ctypes.c_uint64,
                                    ctypes.c_uint64, ctypes.c_int64, i, vp]
     L.momij_profile_enable.argtypes = [i]
@@ -177,6 +179,28 @@ def gqmm2_up_swiglu(x, w, scales, biases, inds, out, *, Ktop: int, K: int, I: in
     return out
 
 
+def ep_dispatch(inds, x, send_x, send_meta, slot_map, status, *, E: int, world: int,
+                capacity: int, stream=None) -> None:
+    """Expert-parallel dispatch (momij_moe_ep_dispatch): packs this rank's
+    (token, slot) pairs into per-destination rows of send_x / send_meta."""
+    M, K = inds.shape
+    H = x.shape[1]
+    _check(lib.momij_moe_ep_dispatch(_ptr(inds), _ptr(x), M, K, E, world, capacity, H, _ptr(send_x),
+                                     _ptr(send_meta), _ptr(slot_map), _ptr(status), _stream(stream)),
+           "epDispatch")
+
+
+def ep_combine(back, scores, slot_map, status, y=None, *, resid_h=None, stream=None) -> None:
+    """Expert-parallel combine (momij_moe_ep_combine) in k order."""
+    M, K = scores.shape
+    H = back.shape[1]
+    out = resid_h if resid_h is not None else y
+    _check(lib.momij_moe_ep_combine(_ptr(back), _ptr(scores), _ptr(slot_map),
+                                    None if resid_h is not None else _ptr(y),
+                                    _ptr(resid_h) if resid_h is not None else None, M, K, H,
+                                    _dtype_code(out), _ptr(status), _stream(stream)), "epCombine")
+
+
 def clamped_swiglu(ug, act, *, I: int, rows: int, clamp: float = 7.0, stream=None):
     _check(lib.momij_moe_clamped_swiglu(_ptr(ug), _ptr(act), rows, I, clamp, _dtype_code(ug),
                                         _stream(stream)), "clampedSwiglu")
@@ -253,18 +277,22 @@ def synth_fill(dst: torch.Tensor, kind: int, *, a: float = 0.0, c: float = 0.0, 
 
 
 def device_expert_weights(E: int, H: int, I: int, gs: int = 64, layer: int = 0, seed: int = 0,
-                          dtype=torch.bfloat16, device="cuda") -> dict:
-    """The tensors of momij_b200.synth.expert_weights, generated on the GPU."""
+                          dtype=torch.bfloat16, device="cuda", experts: tuple | None = None) -> dict:
+    """The tensors of momij_b200.synth.expert_weights, generated on the GPU;
+    experts=(lo, hi) generates only that slice (an expert-parallel shard)."""
     from . import synth as S
     dt = dtype
+    lo, hi = experts if experts is not None else (0, E)
 
     def codes(shape, kind):
-        t = torch.empty(shape, dtype=torch.int32, device=device)
-        return synth_fill(t, 0, seed=seed, stream_id=S.stream_id(layer, kind))
+        per = shape[1] * shape[2]
+        t = torch.empty((hi - lo,) + shape[1:], dtype=torch.int32, device=device)
+        return synth_fill(t, 0, seed=seed, stream_id=S.stream_id(layer, kind), start=lo * per)
 
     def half(shape, kind, a, c):
-        t = torch.empty(shape, dtype=dt, device=device)
-        return synth_fill(t, 1, a=a, c=c, seed=seed, stream_id=S.stream_id(layer, kind))
+        per = shape[1] * shape[2]
+        t = torch.empty((hi - lo,) + shape[1:], dtype=dt, device=device)
+        return synth_fill(t, 1, a=a, c=c, seed=seed, stream_id=S.stream_id(layer, kind), start=lo * per)
 
     return {
         "w_ug": codes((E, 2 * I, H // 16), S.KIND_W_UG),

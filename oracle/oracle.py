@@ -124,6 +124,15 @@ def score_reduce(down, scores, M, Ktop, H, dtype=0):
     return y
 
 
+def score_resid(down, scores, h, M, Ktop, H, dtype=0):
+    """h = cast(h + cast(sum_k score * down)) in k order (maple_score_resid); returns a copy."""
+    h = np.ascontiguousarray(h.copy())
+    lib().oracle_score_resid(_p(np.ascontiguousarray(down), _u16p),
+                             _p(np.ascontiguousarray(scores, np.float32), _f32p), _p(h, _u16p), M, Ktop,
+                             H, dtype)
+    return h
+
+
 def expert_ffn(x, wts: dict, inds, scores, M, H, I, Ktop, gs, clamp=7.0, dtype=0,
                resid_h: np.ndarray | None = None):
     """Returns (y, staged) where staged holds the rounded intermediates."""
