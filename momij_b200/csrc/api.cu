@@ -398,14 +398,16 @@ GemvFn pick_gemv(int dtype, int gs, int mode, int tmax, int stages) {
 
 struct GemvLaunch {
     GemvArgs a;
-    int grid, threads, stages;
+    int grid, threads, stages, tmax;
     size_t smem;
 };
+bool configure_gemv_smem(GemvLaunch& L, int nDG, size_t limit, size_t pt, int gs);
 
 // Worst-case shared-memory sizing from (P, shapes); returns false if the
 // configuration cannot fit on the device.
 bool configure_gemv(GemvLaunch& L, int mode, int tmax, int gs) {
     GemvArgs& a = L.a;
+    L.tmax = tmax;
     const int nK = a.Kd / kChunk;
     a.nK = nK;
     L.threads = kGemvThreads;
@@ -418,15 +420,29 @@ bool configure_gemv(GemvLaunch& L, int mode, int tmax, int gs) {
     if (G > sms) G = sms;
     if (G < 1) G = 1;
     L.grid = (int)G;
-    const long long rows_cta = (Rmax + G - 1) / G;
-    a.max_units = (int)std::min<long long>(a.P, rows_cta / Ru + 2);
-    a.max_tiles = (int)(rows_cta / TR + a.max_units + 1);
-    a.max_vec = a.digit_all_tokens ? a.M : std::min(a.P, a.max_units * tmax);
     const int nDG = a.Kd / kDigitGroup;
-
     const size_t limit = (size_t)max_dyn_smem();
-    const int rt = item_tiles(tmax);
     const size_t pt = 4 * (size_t)((nK + 1) / 2) * tmax * 16;  // red_floats_per_tile
+    // A CTA's slice starts as its share of the worst case; when the slice's
+    // tables and token digits do not fit, slices shrink and each CTA loops
+    // over several (large batches of few tokens per expert).
+    for (long long rows_cta = (Rmax + G - 1) / G; rows_cta >= TR; rows_cta = (rows_cta + 1) / 2) {
+        a.slice_rows = (int)std::min<long long>(rows_cta, 1LL << 30);
+        a.max_units = (int)std::min<long long>(a.P, rows_cta / Ru + 2);
+        a.max_tiles = (int)(rows_cta / TR + a.max_units + 1);
+        a.max_vec = a.digit_all_tokens ? a.M : std::min(a.P, a.max_units * tmax);
+        if (configure_gemv_smem(L, nDG, limit, pt, gs)) return true;
+        if (rows_cta == TR) break;
+    }
+    return false;
+}
+
+// Shared-memory carve-up for the slice bounds in L.a (max_units, max_tiles,
+// max_vec); false if even the smallest ring does not fit.
+bool configure_gemv_smem(GemvLaunch& L, int nDG, size_t limit, size_t pt, int gs) {
+    GemvArgs& a = L.a;
+    const int tmax = L.tmax;
+    const int rt = item_tiles(tmax);
     for (int stages : {4, 2}) {
         size_t off = 0;
         a.off_tiles = (int)off; off += 16 * (size_t)a.max_tiles;
@@ -508,7 +524,9 @@ int tmax_for(int M, int Ktop, int lhs_per_expert) {
     // A token picks an expert at most once under the router; gqmm2 callers
     // may repeat an index inside a token, which the plan splits into more
     // units when it exceeds the bound.
-    return pick_tmax(M < 1 ? 1 : (M > 8 ? 8 : M));
+    // Batches beyond 8 tokens cut units at 4 pairs: the digits of a slice's
+    // two units (8 vectors) then fit in shared memory at H = 4096.
+    return pick_tmax(M < 1 ? 1 : (M > 8 ? 4 : M));
     (void)Ktop;
 }
 

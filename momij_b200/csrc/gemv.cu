@@ -37,8 +37,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     if (a.plan[1] != MOMIJ_OK || U <= 0) return;
     const int Ru = a.rows_per_unit;
     const long long Rtot = (long long)U * Ru;
-    const long long r0 = Rtot * blockIdx.x / gridDim.x, r1 = Rtot * (blockIdx.x + 1) / gridDim.x;
-    if (r0 >= r1) return;
+    // slices of at most slice_rows rows (the shared-memory sizing bound),
+    // at least one per CTA; CTA bx takes slices bx, bx + gridDim.x, ...
+    const long long nsl = max((long long)gridDim.x, (Rtot + a.slice_rows - 1) / a.slice_rows);
 
     int4* s_tiles = reinterpret_cast<int4*>(smem + a.off_tiles);
     int4* s_units = reinterpret_cast<int4*>(smem + a.off_units);
@@ -52,69 +53,81 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
 
     const int32_t* units_g = a.plan + kPlanHeader;
     const int32_t* sorted_g = a.plan + kPlanHeader + 4 * a.P;
+    sb_init(&s_sbar);
+    int sb_par = 0;  // phases of s_sbar completed by earlier slices
+    bool ok = true;
+    __syncthreads();
 
-    if (tid == 0) {
-        const int u_first = (int)(r0 / Ru), u_last = (int)((r1 - 1) / Ru);
-        int nt = 0, nv = 0, over = (u_last - u_first + 1) > a.max_units;
-        if (a.digit_all_tokens) {
-            for (int m = 0; m < a.M; ++m) s_vecs[m] = m;
-            nv = a.M;
-        }
-        for (int u = u_first; u <= u_last && !over; ++u) {
-            const int ul = u - u_first;
-            int4 un = make_int4(units_g[4 * u], units_g[4 * u + 1], units_g[4 * u + 2], 0);
-            s_units[ul] = un;
-            if (un.z > TMAX || (!a.digit_all_tokens && nv + un.z > a.max_vec)) {
-                over = 1;
-                break;
+#pragma unroll 1
+    for (long long sl = blockIdx.x; sl < nsl && ok; sl += gridDim.x) {
+        const long long r0 = Rtot * sl / nsl, r1 = Rtot * (sl + 1) / nsl;
+        if (r0 >= r1) continue;
+        if (tid == 0) {
+            const int u_first = (int)(r0 / Ru), u_last = (int)((r1 - 1) / Ru);
+            int nt = 0, nv = 0, over = (u_last - u_first + 1) > a.max_units;
+            if (a.digit_all_tokens) {
+                for (int m = 0; m < a.M; ++m) s_vecs[m] = m;
+                nv = a.M;
             }
-            for (int j = 0; j < un.z; ++j) {
-                int pr = sorted_g[un.y + j];
-                int vec = a.x_per_pair ? pr : pr / a.Ktop;
-                s_upair[ul * TMAX + j] = pr;
-                if (a.digit_all_tokens) {
-                    s_uslot[ul * TMAX + j] = vec;
-                } else {
-                    s_vecs[nv] = vec;
-                    s_uslot[ul * TMAX + j] = nv++;
+            for (int u = u_first; u <= u_last && !over; ++u) {
+                const int ul = u - u_first;
+                int4 un = make_int4(units_g[4 * u], units_g[4 * u + 1], units_g[4 * u + 2], 0);
+                s_units[ul] = un;
+                if (un.z > TMAX || (!a.digit_all_tokens && nv + un.z > a.max_vec)) {
+                    over = 1;
+                    break;
+                }
+                for (int j = 0; j < un.z; ++j) {
+                    int pr = sorted_g[un.y + j];
+                    int vec = a.x_per_pair ? pr : pr / a.Ktop;
+                    s_upair[ul * TMAX + j] = pr;
+                    if (a.digit_all_tokens) {
+                        s_uslot[ul * TMAX + j] = vec;
+                    } else {
+                        s_vecs[nv] = vec;
+                        s_uslot[ul * TMAX + j] = nv++;
+                    }
+                }
+                long long lo = max(r0, (long long)u * Ru) - (long long)u * Ru;
+                long long hi = min(r1, (long long)(u + 1) * Ru) - (long long)u * Ru;
+                for (long long rs = lo; rs < hi && !over; rs += TR) {
+                    if (nt >= a.max_tiles) { over = 1; break; }
+                    s_tiles[nt++] = make_int4(ul, (int)rs, (int)min((long long)TR, hi - rs), 0);
                 }
             }
-            long long lo = max(r0, (long long)u * Ru) - (long long)u * Ru;
-            long long hi = min(r1, (long long)(u + 1) * Ru) - (long long)u * Ru;
-            for (long long rs = lo; rs < hi && !over; rs += TR) {
-                if (nt >= a.max_tiles) { over = 1; break; }
-                s_tiles[nt++] = make_int4(ul, (int)rs, (int)min((long long)TR, hi - rs), 0);
-            }
+            s_ntiles = nt;
+            s_nvec = nv;
+            s_overflow = over;
         }
-        s_ntiles = nt;
-        s_nvec = nv;
-        s_overflow = over;
-    }
-    __syncthreads();
-    // capacity guard: the host sizes shared memory from worst-case bounds, so
-    // this never triggers for valid plans; if it does, the error word is set
-    // and nothing is written
-    if (s_overflow) {
-        if (tid == 0) atomicExch(a.plan + 2, MOMIJ_ERR_WORKSPACE);
-        return;
-    }
+        __syncthreads();
+        // capacity guard: the host sizes shared memory from worst-case bounds, so
+        // this never triggers for valid plans; if it does, the error word is set
+        // and nothing more is written
+        if (s_overflow) {
+            if (tid == 0) atomicExch(a.plan + 2, MOMIJ_ERR_WORKSPACE);
+            break;
+        }
 
-    PhaseTables tabs{s_tiles, s_units, s_uslot, s_ntiles};
-    PhaseWeights wts{a.w, a.s, a.b, a.N, a.rows_per_unit, a.Kd};
-    sb_init(&s_sbar);
-    GemvPhase<DT, GS, MODE, TMAX, STAGES> ph(tabs, wts, s_stage, 0, a.nK,
-                                             reinterpret_cast<uint16_t*>(smem + a.off_sb), a.batch_tiles,
-                                             &s_sbar);
-    auto ahead = [&]() { ph.load_next(); };
-    bar_sync(kBarConsumers, kConsumerThreads);  // the scale/bias mbarrier is initialised
-    if (s_ntiles > 0) ph.issue_sb(0, min(s_ntiles, a.batch_tiles));
-    ph.prefetch(ahead);
-    // encode the activations while the first items land
-    digitize<DT>(a.x, s_vecs, s_nvec, a.Kd, s_dig, s_fs, kConsumerThreads);
-    bar_sync(kBarConsumers, kConsumerThreads);
-    StoreOut<DT, MODE, TMAX> out{s_upair, a.out, a.out_cols, a.clamp};
-    const bool ok = ph.consume(s_dig, s_fs, s_red, true, out, ahead);
-    ring_quiesce();
+        PhaseTables tabs{s_tiles, s_units, s_uslot, s_ntiles};
+        PhaseWeights wts{a.w, a.s, a.b, a.N, a.rows_per_unit, a.Kd};
+        GemvPhase<DT, GS, MODE, TMAX, STAGES> ph(tabs, wts, s_stage, 0, a.nK,
+                                                 reinterpret_cast<uint16_t*>(smem + a.off_sb), a.batch_tiles,
+                                                 &s_sbar);
+        ph.sb_par = sb_par;
+        auto ahead = [&]() { ph.load_next(); };
+        if (s_ntiles > 0) ph.issue_sb(0, min(s_ntiles, a.batch_tiles));
+        ph.prefetch(ahead);
+        // encode the activations while the first items land
+        digitize<DT>(a.x, s_vecs, s_nvec, a.Kd, s_dig, s_fs, kConsumerThreads);
+        bar_sync(kBarConsumers, kConsumerThreads);
+        StoreOut<DT, MODE, TMAX> out{s_upair, a.out, a.out_cols, a.clamp};
+        const bool done = ph.consume(s_dig, s_fs, s_red, true, out, ahead);
+        ring_quiesce();
+        sb_par = ph.sb_par;
+        // this slice's tables, digits and ring are free again; a bounded wait
+        // that gave up in any thread ends the loop in all of them
+        ok = __syncthreads_and(done ? 1 : 0) != 0;
+    }
     if (!ok && tid == 0) atomicExch(a.plan + 2, MOMIJ_ERR_TIMEOUT);
     pdl_launch_dependents();
 }

@@ -23,6 +23,7 @@ struct GemvArgs {
     float clamp;
     int nK;              // 256-code chunks per row
     int max_units, max_tiles, max_vec;
+    int slice_rows;      // cap on the (unit, row) slice a CTA handles at once (it loops over slices)
     int batch_tiles;     // tiles per epilogue batch (a multiple of item_tiles): red and scale buffers
     // dynamic shared-memory carve-up (byte offsets)
     int off_tiles, off_units, off_upair, off_uslot, off_vecs, off_fs, off_dig, off_red, off_sb, off_stage;
