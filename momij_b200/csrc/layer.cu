@@ -461,16 +461,21 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
             const int m = rem / rowsmax, r = rem % rowsmax;
             const int n = s_last[q] * 64 + r;
             if (n >= a.H) continue;
-            // all K loads first (independent), then the fp32 sum in k order
-            float dv[32];
-#pragma unroll
-            for (int k = 0; k < 32; ++k)
-                dv[k] = (k < a.K) ? Half<DT>::to_f(__ldcg(a.down + (size_t)(m * a.K + k) * a.H + n))
-                                  : 0.f;
+            // per 8 slots: the loads first (independent), then the fp32 sum in
+            // k order (a short loop keeps the kernel's code small)
             float acc = 0.f;
+#pragma unroll 1
+            for (int k0 = 0; k0 < a.K; k0 += 8) {
+                float dv[8];
 #pragma unroll
-            for (int k = 0; k < 32; ++k)
-                if (k < a.K) acc = fmaf(dv[k], s_scores[m * a.K + k], acc);
+                for (int k = 0; k < 8; ++k)
+                    dv[k] = (k0 + k < a.K)
+                                ? Half<DT>::to_f(__ldcg(a.down + (size_t)(m * a.K + k0 + k) * a.H + n))
+                                : 0.f;
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (k0 + k < a.K) acc = fmaf(dv[k], s_scores[m * a.K + k0 + k], acc);
+            }
             const size_t off = (size_t)m * a.H + n;
             if (a.h) {
                 const float delta = Half<DT>::to_f(Half<DT>::from_f(acc));
