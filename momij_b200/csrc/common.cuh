@@ -107,7 +107,7 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
-// ---- mbarriers and TMA bulk copies (no multicast) ---------------------------
+// ---- mbarriers and TMA bulk copies (each into this CTA only) ----------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count)
                  : "memory");
