@@ -608,20 +608,30 @@ int run_grouped(const void* x, const uint32_t* w_ug, const void* s_ug, const voi
     // the block list is read as int4 entries: 16-byte aligned (the region has 4 ints of slack)
     int32_t* blocks = reinterpret_cast<int32_t*>(align_up(reinterpret_cast<uintptr_t>(weight + P), 16));
     if (cudaMemsetAsync(hdr + 1, 0, sizeof(int32_t), st) != cudaSuccess) return MOMIJ_ERR_CUDA;
+    const int G = current_device_sm_count();
+    if (G <= 0) return MOMIJ_ERR_CUDA;
     int slot = prof_begin(MOMIJ_KERNEL_PLAN, st);
-    int rc = cuda_status(launch(permute_kernel, dim3(1), dim3(1024), sizeof(int) * (E + 1), st, inds,
-                                scores, P, E, offsets, pair, weight, hdr + 1));
+    int rc = cuda_status(launch(permute_kernel, dim3(std::min(E, 2 * G)), dim3(kPermuteThreads),
+                                sizeof(int) * (E + 1), st, inds, scores, P, E, offsets, pair, weight, hdr + 1));
     if (!rc) rc = cuda_status(launch(block_list_kernel, dim3(1), dim3(32), 0, st,
                                      static_cast<const int32_t*>(offsets), E, blocks,
                                      static_cast<const int32_t*>(hdr + 1)));
     prof_end(slot, st);
     if (rc) return rc;
-    const int G = current_device_sm_count();
-    if (G <= 0) return MOMIJ_ERR_CUDA;
-    const size_t smem = 3 * (2 * 128 * 128 + kBlockTokens * 128) + 1024;  // 3 stages x (A hi, A lo, B)
+    const size_t smem = grouped_smem_bytes();
+    // The GEMMs run along K in class order (the dequantised weight tiles'
+    // order): the tokens are reordered into the down buffer (free until the
+    // down GEMM, M <= P rows) and the up GEMM writes act in that order.
+    {
+        const long long blocks16 = (long long)M * H / 16;
+        const int nb = (int)std::min<long long>((blocks16 + 255) / 256, 4L * G);
+        rc = cuda_status(launch(class_order_kernel, dim3(nb > 0 ? nb : 1), dim3(256), 0, st,
+                                static_cast<const uint4*>(x), reinterpret_cast<uint4*>(ws.down), blocks16));
+        if (rc) return rc;
+    }
     for (int mode : {kModeUpSwiglu, kModeRows}) {
         GroupedArgs a{};
-        a.x = static_cast<const uint16_t*>(mode == kModeUpSwiglu ? x : ws.act);
+        a.x = static_cast<const uint16_t*>(mode == kModeUpSwiglu ? ws.down : ws.act);
         a.x_per_pair = mode == kModeUpSwiglu ? 0 : 1;
         a.w = mode == kModeUpSwiglu ? w_ug : w_dn;
         a.s = static_cast<const uint16_t*>(mode == kModeUpSwiglu ? s_ug : s_dn);
@@ -769,7 +779,12 @@ int momij_moe_permute(const int32_t* inds, const float* scores, int M, int K, in
         return MOMIJ_ERR_INVALID_ARGUMENT;
     if (E > 8192) return MOMIJ_ERR_UNSUPPORTED_SHAPE;
     const size_t smem = sizeof(int) * (E + 1);
-    return cuda_status(launch(permute_kernel, dim3(1), dim3(1024), smem,
+    const int G = current_device_sm_count();
+    if (G <= 0) return MOMIJ_ERR_CUDA;
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return MOMIJ_ERR_CUDA;
+    return cuda_status(launch(permute_kernel, dim3(std::min(E, 2 * G)), dim3(kPermuteThreads), smem,
                               static_cast<cudaStream_t>(stream), inds, scores, M * K, E, offsets,
                               pair, weight, static_cast<int32_t*>(nullptr)));
 }

@@ -34,6 +34,7 @@ __global__ void route_kernel(const float* logits, int M, int E, int K, int32_t* 
 __global__ void plan_kernel(const int32_t* inds, int P, int E, int tmax, int32_t* plan, int allow_pad);
 __global__ void route_plan_kernel(const float* logits, int M, int E, int K, int tmax,
                                   int32_t* inds, float* scores, int32_t* plan);
+constexpr int kPermuteThreads = 256;
 __global__ void permute_kernel(const int32_t* inds, const float* scores, int P, int E,
                                int32_t* offsets, int32_t* pair, float* weight, int32_t* status);
 

@@ -9,11 +9,18 @@
 // dequantised (w = s*q + b in fp32) and split into two activation-dtype tiles
 // A_hi = round(w) and A_lo = round(w - A_hi), so A_hi + A_lo carries w to
 // ~2^-17 (a single 16-bit rounding of w would cost ~2^-9 per weight, several
-// times the tolerance after two projections); B = the block's token rows
-// gathered with cp.async.  One thread issues eight tcgen05.mma.kind::f16
-// (M=128, N=tokens rounded up to 16, K=16; hi then lo into the same fp32
-// accumulator) per k-block and commits them to the stage's mbarrier; the
-// other threads fill the other stage meanwhile.  The epilogue reads TMEM (tcgen05.ld) and writes per-pair
+// times the tolerance after two projections); B = the block's token rows.
+// The four values a (row, group) can take are tabulated once per k-block and
+// codes become packed halves by byte permutes, four codes of one bit
+// position ("class") at a time, so the tiles hold each 16-element block of K
+// in class order (element 4j + p at 4p + j) and the activations are reordered
+// alike (class_order_kernel; the up GEMM writes act in that order).
+// Pipeline per CTA: a ring of load stages (token rows, codes, scale and bias
+// words) filled by cp.async four k-blocks ahead, two slots of dequantised A;
+// one thread issues eight tcgen05.mma.kind::f16 (M=128, N=tokens rounded up
+// to 16, K=16; hi then lo into the same fp32 accumulator) per k-block and
+// commits them to the slot's mbarrier while the other threads dequantise the
+// next k-block.  The epilogue reads TMEM (tcgen05.ld) and writes per-pair
 // rows: the staged clamped SwiGLU of up||gate (tile = 64 up rows + the
 // matching 64 gate rows), or the down projection.
 //
@@ -29,11 +36,25 @@ namespace momij {
 
 namespace {
 
+// Shared memory: a ring of kLoadStages load stages (per k-block: the token
+// rows B in the MMA layout, the 128 weight rows' codes, and the 4-byte words
+// holding their scales and biases), copied kLoadAhead k-blocks ahead with
+// cp.async, and two slots of dequantised weights (A hi, A lo) that alternate
+// between the dequantising threads and the tensor core.
 constexpr int kStageA = 128 * 128;           // 128 weight rows x 64 elements x 2 B (one of hi / lo)
+constexpr int kSlotA = 2 * kStageA;          // A hi + A lo
+constexpr int kASlots = 2;
 constexpr int kStageB = kBlockTokens * 128;  // tokens x 64 elements x 2 B
-constexpr int kStageBytes = 2 * kStageA + kStageB;
-constexpr int kStages = 3;  // k-block stages: B of k-block kb+1 loads while kb is dequantised and kb-1 multiplies
+constexpr int kLoadCodes = kStageB;          // 128 rows x 16 B of codes
+constexpr int kLoadScales = kLoadCodes + 128 * 16;
+constexpr int kLoadBiases = kLoadScales + 128 * 4;
+constexpr int kLoadBytes = kLoadBiases + 128 * 4;  // 19456 = 19 KB (a multiple of 1024)
+constexpr int kLoadStages = 6;
+constexpr int kLoadAhead = kLoadStages - 2;  // a stage is refilled once the MMAs of two k-blocks ago are done
 constexpr int kTmemCols = kBlockTokens;      // fp32 accumulator columns
+static_assert(kLoadBytes % 1024 == 0 && kSlotA % 1024 == 0, "stages keep the 1024-B swizzle alignment");
+static_assert(grouped_smem_bytes() == (size_t)kASlots * kSlotA + (size_t)kLoadStages * kLoadBytes + 1024,
+              "host and kernel agree on the shared-memory size");
 constexpr int kMmaWaitLimit = 1 << 24;
 
 // tcgen05 shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row
@@ -69,6 +90,11 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     else
         asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     return r;
+}
+// Column of element c in class order: within each block of 16 elements,
+// element 4j + p moves to 4p + j (the order the dequantised weight tiles use).
+__device__ __forceinline__ int class_order16(int c) {
+    return (c & ~15) | ((c & 3) << 2) | ((c >> 2) & 3);
 }
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
     asm volatile(
@@ -116,13 +142,38 @@ __global__ void block_list_kernel(const int32_t* offsets, int E, int32_t* blocks
     pdl_launch_dependents();
 }
 
+// y = x with every row's 16-element blocks in class order (class_order16);
+// one thread per block of 16 halves.
+__global__ void class_order_kernel(const uint4* __restrict__ x, uint4* __restrict__ y, long long blocks) {
+    pdl_wait();
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < blocks;
+         i += (long long)gridDim.x * blockDim.x) {
+        const uint4 u = x[2 * i], v = x[2 * i + 1];
+        const uint32_t w[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
+        uint32_t o[8];
+#pragma unroll
+        for (int p = 0; p < 4; ++p)
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+                // output halves 4p + 2jj, 4p + 2jj + 1 <- elements 4 (2jj) + p, 4 (2jj + 1) + p
+                const int e0 = 8 * jj + p, e1 = 8 * jj + 4 + p;
+                const uint32_t h0 = (w[e0 >> 1] >> (16 * (e0 & 1))) & 0xffffu;
+                const uint32_t h1 = (w[e1 >> 1] >> (16 * (e1 & 1))) & 0xffffu;
+                o[2 * p + jj] = h0 | (h1 << 16);
+            }
+        y[2 * i] = make_uint4(o[0], o[1], o[2], o[3]);
+        y[2 * i + 1] = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+    pdl_launch_dependents();
+}
+
 template <int DT, int GS, int MODE>
 __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const GroupedArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ uint32_t s_tmem;
-    __shared__ __align__(8) uint64_t s_bar[kStages];
+    __shared__ __align__(8) uint64_t s_bar[kASlots];  // MMA completion per A slot
     __shared__ int s_pair[kBlockTokens], s_row[kBlockTokens];
     __shared__ int s_timeout;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -144,7 +195,7 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) mbar_init(&s_bar[s], 1);
+        for (int s = 0; s < kASlots; ++s) mbar_init(&s_bar[s], 1);
         mbar_fence_init();
         s_timeout = 0;
     }
@@ -153,8 +204,8 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
     tc_fence_after();
     const uint32_t tmem = s_tmem;
 
-    uint32_t phase[kStages] = {0u, 0u, 0u};
-    bool pending[kStages] = {false, false, false};
+    uint32_t phase[kASlots] = {0u, 0u};
+    bool pending[kASlots] = {false, false};
     auto wait_stage = [&](int s) {
         bool ok = false;
         for (int it = 0; it < kMmaWaitLimit && !ok; ++it) ok = mbar_try_wait(&s_bar[s], phase[s]);
@@ -184,62 +235,87 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
             s_pair[tid] = p;
             s_row[tid] = a.x_per_pair ? p : p / a.Ktop;
         }
-        int grow;
-        if (MODE == kModeUpSwiglu) grow = (ra < 64) ? rb * 64 + ra : a.Ru + rb * 64 + (ra - 64);
-        else grow = rb * 128 + ra;
-        const size_t wrow = (size_t)e * a.N + grow;
-        const uint32_t* wp = a.w + wrow * (size_t)(a.Kd / 16) + half * 2;
-        const uint16_t* sp = a.s + wrow * nsb;
-        const uint16_t* bp = a.b + wrow * nsb;
-        uint2 cw = *reinterpret_cast<const uint2*>(wp);
-        uint16_t cs = sp[0], cb = bp[0];
         __syncthreads();  // s_row ready; the previous tile's epilogue is done with shared memory
+        unsigned char* const ring = smem + kASlots * kSlotA;
 
-        // token rows of k-block kb into stage st (its previous MMAs are done)
-        auto issue_b = [&](int kb, int st) {
-            unsigned char* sB = smem + st * kStageBytes + 2 * kStageA;
+        // k-block kb's load stage: token rows (MMA layout), the codes of the
+        // 128 rows (thread r < 128: row r) and the words holding their
+        // group's scale and bias (nsb is even, so the word is 4-B aligned)
+        auto issue_load = [&](int kb) {
+            unsigned char* st = ring + (kb % kLoadStages) * kLoadBytes;
             for (int i = tid; i < nmma * 8; i += kGroupedThreads) {
                 const int n = i >> 3, part = i & 7;
                 const bool v = n < cnt;
                 const uint16_t* src = a.x + (size_t)(v ? s_row[n] : 0) * a.Kd + kb * 64 + part * 8;
-                cp_async16(smem_u32(sB + sw128(n, part * 8)), src, v);
+                cp_async16(smem_u32(st + sw128(n, part * 8)), src, v);
+            }
+            if (tid < 128) {
+                int gr;
+                if (MODE == kModeUpSwiglu) gr = (tid < 64) ? rb * 64 + tid : a.Ru + rb * 64 + (tid - 64);
+                else gr = rb * 128 + tid;
+                const size_t row = (size_t)e * a.N + gr;
+                cp_async16(smem_u32(st + kLoadCodes + tid * 16), a.w + row * (size_t)(a.Kd / 16) + kb * 4, true);
+                const size_t gw = row * nsb + (((size_t)kb * 64 / GS) & ~(size_t)1);
+                cp_async4(smem_u32(st + kLoadScales + tid * 4), a.s + gw, true);
+                cp_async4(smem_u32(st + kLoadBiases + tid * 4), a.b + gw, true);
             }
         };
-        issue_b(0, 0);
-        cp_async_commit();
+#pragma unroll 1
+        for (int kb = 0; kb < kLoadAhead; ++kb) {
+            if (kb < KB) issue_load(kb);
+            cp_async_commit();  // one group per k-block (possibly empty)
+        }
+        // k-block 0's stage has landed for every thread
+        cp_async_wait<kLoadAhead - 1>();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
 
 #pragma unroll 1
         for (int kb = 0; kb < KB; ++kb) {
-            const int s = kb % kStages;
-            if (kb + 1 < KB) {  // next k-block's token rows into the stage of k-block kb - 2
-                const int sn = (kb + 1) % kStages;
-                if (pending[sn]) wait_stage(sn);
-                issue_b(kb + 1, sn);
-            }
-            cp_async_commit();  // one group per k-block (possibly empty)
-            unsigned char* sA = smem + s * kStageBytes;  // hi
-            unsigned char* sL = sA + kStageA;             // lo
-            unsigned char* sB = sL + kStageA;
+            const int s = kb % kASlots;
+            // the MMAs of k-block kb - 2 used A slot s and load stage (kb + kLoadAhead) % kLoadStages
+            if (pending[s]) wait_stage(s);
+            if (kb + kLoadAhead < KB) issue_load(kb + kLoadAhead);
+            cp_async_commit();
+            unsigned char* st = ring + (kb % kLoadStages) * kLoadBytes;
+            unsigned char* sA = smem + s * kSlotA;  // hi
+            unsigned char* sL = sA + kStageA;        // lo
+            unsigned char* sB = st;
             {
-                const float sc = Half<DT>::to_f(cs), bi2 = Half<DT>::to_f(cb);
+                const uint2 cw = *reinterpret_cast<const uint2*>(st + kLoadCodes + ra * 16 + half * 8);
+                const int gsel = ((kb * 64) / GS) & 1;
+                const uint32_t sw = *reinterpret_cast<const uint32_t*>(st + kLoadScales + ra * 4);
+                const uint32_t bw = *reinterpret_cast<const uint32_t*>(st + kLoadBiases + ra * 4);
+                const float sc = Half<DT>::to_f((uint16_t)(gsel ? sw >> 16 : sw & 0xffffu));
+                const float bi2 = Half<DT>::to_f((uint16_t)(gsel ? bw >> 16 : bw & 0xffffu));
                 const uint32_t c2[2] = {cw.x, cw.y};
-                if (kb + 1 < KB) {  // the next k-block's codes, scale and bias are in flight meanwhile
-                    cw = *reinterpret_cast<const uint2*>(wp + (kb + 1) * 4);
-                    const int g1 = ((kb + 1) * 64) / GS;
-                    cs = sp[g1];
-                    cb = bp[g1];
+                // The row's group takes four weight values w_q = s*q + b: their
+                // hi and lo halves as byte tables (low bytes, high bytes), so a
+                // byte permute turns two codes into two packed halves.
+                uint32_t thA = 0, thB = 0, tlA = 0, tlB = 0;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float w = fmaf(sc, (float)q, bi2);
+                    const uint32_t hl = pack2<DT>(w, w - Half<DT>::to_f(Half<DT>::from_f(w)));
+                    thA |= (hl & 0xffu) << (8 * q);
+                    thB |= ((hl >> 8) & 0xffu) << (8 * q);
+                    tlA |= ((hl >> 16) & 0xffu) << (8 * q);
+                    tlB |= (hl >> 24) << (8 * q);
                 }
 #pragma unroll
                 for (int word = 0; word < 2; ++word) {
+                    // class order within the 16 codes of the word: column 4p + j
+                    // holds code 4j + p (the activations are permuted alike)
                     uint32_t hi[8], lo[8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const float q0 = (float)((c2[word] >> (4 * i)) & 3u);
-                        const float q1 = (float)((c2[word] >> (4 * i + 2)) & 3u);
-                        const float w0 = fmaf(sc, q0, bi2), w1 = fmaf(sc, q1, bi2);
-                        hi[i] = pack2<DT>(w0, w1);
-                        lo[i] = pack2<DT>(w0 - Half<DT>::to_f((uint16_t)(hi[i] & 0xffffu)),
-                                          w1 - Half<DT>::to_f((uint16_t)(hi[i] >> 16)));
+                    for (int p = 0; p < 4; ++p) {
+                        const uint32_t m = (c2[word] >> (2 * p)) & 0x03030303u;  // byte j: code 4j + p
+                        const uint32_t sel = m | (m << 4) | 0x40404040u;         // nibbles (q, q + 4) per code
+                        const uint32_t sel2 = sel >> 16;
+                        hi[2 * p] = __byte_perm(thA, thB, sel);
+                        hi[2 * p + 1] = __byte_perm(thA, thB, sel2);
+                        lo[2 * p] = __byte_perm(tlA, tlB, sel);
+                        lo[2 * p + 1] = __byte_perm(tlA, tlB, sel2);
                     }
                     const int k0 = half * 32 + word * 16;
                     const uint32_t o0 = sw128(ra, k0), o1 = sw128(ra, k0 + 8);
@@ -249,8 +325,11 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
                     *reinterpret_cast<uint4*>(sL + o1) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
                 }
             }
-            cp_async_wait<1>();  // this k-block's token rows (the next k-block's may be in flight)
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
+            // the next k-block's load stage has landed (this thread's copies;
+            // the barrier publishes everyone's), and this k-block's A tiles are
+            // written: both become visible to the tensor core
+            cp_async_wait<kLoadAhead - 1>();
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncthreads();
             if (tid == 0) {
                 tc_fence_after();
@@ -274,7 +353,7 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
             }
             pending[s] = true;
         }
-        for (int s = 0; s < kStages; ++s)
+        for (int s = 0; s < kASlots; ++s)
             if (pending[s]) wait_stage(s);
         tc_fence_after();
 
@@ -283,7 +362,7 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
         const int r = 32 * (warp & 3) + lane;  // A row = TMEM lane
         const int c0 = 64 * (warp >> 2);
         if (MODE == kModeUpSwiglu) {
-            float* sG = reinterpret_cast<float*>(smem);  // [token][64] gate sums (stage 0 is free)
+            float* sG = reinterpret_cast<float*>(smem);  // [token][64] gate sums (the A slots are free)
             if (r >= 64) {
 #pragma unroll 1
                 for (int cc = 0; cc < 64; cc += 16) {
@@ -303,8 +382,8 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int n = c0 + cc + j;
-                        if (n < cnt)
-                            a.out[(size_t)s_pair[n] * a.Ru + rb * 64 + r] =
+                        if (n < cnt)  // act columns in class order for the down GEMM
+                            a.out[(size_t)s_pair[n] * a.Ru + class_order16(rb * 64 + r)] =
                                 swiglu_staged<DT>(__uint_as_float(v[j]), sG[n * 64 + r], a.clamp);
                     }
                 }

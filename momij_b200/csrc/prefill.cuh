@@ -20,8 +20,12 @@ __host__ __device__ constexpr size_t block_list_ints(int P, int E) {
     return kBlockHeader + 4 * ((size_t)P / kBlockTokens + (size_t)E + 1);
 }
 
+// Dynamic shared memory of grouped_gemm_kernel: two slots of dequantised
+// weights (hi + lo, 32 KB each), six 19-KB load stages, 1 KB of alignment.
+__host__ __device__ constexpr size_t grouped_smem_bytes() { return 2 * 32768 + 6 * 19456 + 1024; }
+
 struct GroupedArgs {
-    const uint16_t* x;       // activation rows [rows, Kd]
+    const uint16_t* x;       // activation rows [rows, Kd], 16-element blocks in class order
     int x_per_pair;          // 1: row of pair p is p; 0: p / Ktop
     const uint32_t* w;       // [E, N, Kd/16]
     const uint16_t* s;       // [E, N, Kd/gs]
@@ -30,11 +34,16 @@ struct GroupedArgs {
     const int32_t* pairs;    // sorted pair ids
     int32_t* status;         // work-plan header: [1] routing status, [2] error word (both 0: run);
                              // a stuck MMA wait records MOMIJ_ERR_TIMEOUT in [2]
-    uint16_t* out;           // up||gate mode: act [P, Ru]; rows mode: [P, N]
+    uint16_t* out;           // up||gate mode: act [P, Ru] (columns in class order); rows mode: [P, N]
     int Kd, N, Ru, Ktop;     // Ru: up||gate mode: first gate row (= I)
     int E, P;                // experts, pairs (bounds of the block list entries)
     float clamp;
 };
+
+// y = x with each row's 16-element blocks in class order (element 4j + p of
+// a block at 4p + j), the K order of the dequantised weight tiles; `blocks`
+// = rows * K / 16.
+__global__ void class_order_kernel(const uint4* x, uint4* y, long long blocks);
 
 // Builds the block list from the per-expert offsets of permute_kernel.
 __global__ void block_list_kernel(const int32_t* offsets, int E, int32_t* blocks,

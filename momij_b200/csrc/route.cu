@@ -129,68 +129,82 @@ __global__ void __launch_bounds__(1024) route_plan_kernel(const float* __restric
 }
 
 // ---- per-expert token lists (counting sort, stable in the pair index) ----
-// One block; warp w owns experts w, w+32, ...; each scans the P pairs in
-// order with ballots, so positions are deterministic.
-__global__ void __launch_bounds__(1024) permute_kernel(const int32_t* __restrict__ inds,
-                                                       const float* __restrict__ scores, int P,
-                                                       int E, int32_t* __restrict__ offsets,
-                                                       int32_t* __restrict__ pair,
-                                                       float* __restrict__ weight,
-                                                       int32_t* __restrict__ status) {
+// Every block histograms all P indices in shared memory and scans the counts
+// (so each knows every expert's offset), then collects the pairs of experts
+// blockIdx.x, blockIdx.x + gridDim.x, ... in pair order with block-wide
+// ballots: positions are deterministic whatever the grid size.  Block 0
+// writes the offsets [E + 1].
+__global__ void __launch_bounds__(kPermuteThreads) permute_kernel(const int32_t* __restrict__ inds,
+                                                                  const float* __restrict__ scores, int P,
+                                                                  int E, int32_t* __restrict__ offsets,
+                                                                  int32_t* __restrict__ pair,
+                                                                  float* __restrict__ weight,
+                                                                  int32_t* __restrict__ status) {
     extern __shared__ int s_cnt[];  // E + 1
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    constexpr int kWarps = kPermuteThreads / 32;
     __shared__ int s_bad;
+    __shared__ int s_wsum[kWarps];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     pdl_wait();  // the indices may come from the previous kernel on the stream
-    if (threadIdx.x == 0) s_bad = 0;
+    if (tid == 0) s_bad = 0;
+    for (int e = tid; e <= E; e += kPermuteThreads) s_cnt[e] = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < P; i += blockDim.x) {
-        int e = inds[i];
+    for (int i = tid; i < P; i += kPermuteThreads) {
+        const int e = inds[i];
         if (e < 0 || e >= E) s_bad = 1;
+        else atomicAdd(&s_cnt[e], 1);
     }
     __syncthreads();
     if (s_bad) {
-        if (threadIdx.x == 0 && status) *status = MOMIJ_ERR_EXPERT_INDEX;
+        if (blockIdx.x == 0 && tid == 0 && status) *status = MOMIJ_ERR_EXPERT_INDEX;
         return;
     }
-    for (int e = warp; e < E; e += nw) {
-        int c = 0;
-        for (int base = 0; base < P; base += 32) {
-            int i = base + lane;
-            c += __popc(__ballot_sync(0xffffffffu, i < P && inds[i] == e));
-        }
-        if (lane == 0) s_cnt[e] = c;
-    }
-    __syncthreads();
-    if (warp == 0) {
+    if (warp == 0) {  // exclusive scan of the counts, in place; s_cnt[E] = P
         int carry = 0;
         for (int base = 0; base < E; base += 32) {
-            int e = base + lane;
-            int v = e < E ? s_cnt[e] : 0, incl = v;
+            const int e = base + lane;
+            const int v = e < E ? s_cnt[e] : 0;
+            int incl = v;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
-                int y = __shfl_up_sync(0xffffffffu, incl, o);
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
                 if (lane >= o) incl += y;
             }
-            if (e < E) offsets[e] = carry + incl - v;
+            if (e < E) s_cnt[e] = carry + incl - v;
             carry += __shfl_sync(0xffffffffu, incl, 31);
         }
-        if (lane == 0) offsets[E] = carry;
+        if (lane == 0) s_cnt[E] = carry;
     }
     __syncthreads();
-    for (int e = warp; e < E; e += nw) {
-        int pos = offsets[e];
-        for (int base = 0; base < P; base += 32) {
-            int i = base + lane;
-            bool hit = i < P && inds[i] == e;
-            uint32_t m = __ballot_sync(0xffffffffu, hit);
+    if (blockIdx.x == 0)
+        for (int e = tid; e <= E; e += kPermuteThreads) offsets[e] = s_cnt[e];
+    const unsigned below = (1u << lane) - 1u;
+    for (int e = blockIdx.x; e < E; e += gridDim.x) {
+        int pos = s_cnt[e];
+        const int end = s_cnt[e + 1];
+        for (int base = 0; base < P && pos < end; base += kPermuteThreads) {
+            const int i = base + tid;
+            const bool hit = i < P && inds[i] == e;
+            const unsigned m = __ballot_sync(0xffffffffu, hit);
+            if (lane == 0) s_wsum[warp] = __popc(m);
+            __syncthreads();
+            int before = 0, total = 0;
+#pragma unroll
+            for (int w = 0; w < kWarps; ++w) {
+                const int c = s_wsum[w];
+                before += w < warp ? c : 0;
+                total += c;
+            }
             if (hit) {
-                int q = pos + __popc(m & ((1u << lane) - 1u));
+                const int q = pos + before + __popc(m & below);
                 pair[q] = i;
                 weight[q] = scores[i];
             }
-            pos += __popc(m);
+            pos += total;
+            __syncthreads();
         }
     }
+    pdl_launch_dependents();
 }
 
 }  // namespace momij
