@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
 
     const int KB = a.Kd / 64;
     const int nsb = a.Kd / GS;
-    const int ra = tid >> 1, half = tid & 1;  // this thread dequantises row ra, codes half*32 + [0, 32)
+    const int ra = tid >> 2, wq = tid & 3;  // this thread dequantises row ra, codes 16 wq + [0, 16)
     const int4* blist = reinterpret_cast<const int4*>(a.blocks + kBlockHeader);
 
 #pragma unroll 1
@@ -249,15 +249,19 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
                 const uint16_t* src = a.x + (size_t)(v ? s_row[n] : 0) * a.Kd + kb * 64 + part * 8;
                 cp_async16(smem_u32(st + sw128(n, part * 8)), src, v);
             }
-            if (tid < 128) {
+            if (tid < 3 * 128) {  // thread 128 j + r: row r's codes (j = 0), scale word (1) or bias word (2)
+                const int j = tid >> 7, rr = tid & 127;
                 int gr;
-                if (MODE == kModeUpSwiglu) gr = (tid < 64) ? rb * 64 + tid : a.Ru + rb * 64 + (tid - 64);
-                else gr = rb * 128 + tid;
+                if (MODE == kModeUpSwiglu) gr = (rr < 64) ? rb * 64 + rr : a.Ru + rb * 64 + (rr - 64);
+                else gr = rb * 128 + rr;
                 const size_t row = (size_t)e * a.N + gr;
-                cp_async16(smem_u32(st + kLoadCodes + tid * 16), a.w + row * (size_t)(a.Kd / 16) + kb * 4, true);
-                const size_t gw = row * nsb + (((size_t)kb * 64 / GS) & ~(size_t)1);
-                cp_async4(smem_u32(st + kLoadScales + tid * 4), a.s + gw, true);
-                cp_async4(smem_u32(st + kLoadBiases + tid * 4), a.b + gw, true);
+                if (j == 0) {
+                    cp_async16(smem_u32(st + kLoadCodes + rr * 16), a.w + row * (size_t)(a.Kd / 16) + kb * 4, true);
+                } else {
+                    const size_t gw = row * nsb + (((size_t)kb * 64 / GS) & ~(size_t)1);
+                    cp_async4(smem_u32(st + (j == 1 ? kLoadScales : kLoadBiases) + rr * 4), (j == 1 ? a.s : a.b) + gw,
+                              true);
+                }
             }
         };
 #pragma unroll 1
@@ -282,48 +286,43 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
             unsigned char* sL = sA + kStageA;        // lo
             unsigned char* sB = st;
             {
-                const uint2 cw = *reinterpret_cast<const uint2*>(st + kLoadCodes + ra * 16 + half * 8);
+                const uint32_t cw = *reinterpret_cast<const uint32_t*>(st + kLoadCodes + ra * 16 + wq * 4);
                 const int gsel = ((kb * 64) / GS) & 1;
                 const uint32_t sw = *reinterpret_cast<const uint32_t*>(st + kLoadScales + ra * 4);
                 const uint32_t bw = *reinterpret_cast<const uint32_t*>(st + kLoadBiases + ra * 4);
                 const float sc = Half<DT>::to_f((uint16_t)(gsel ? sw >> 16 : sw & 0xffffu));
                 const float bi2 = Half<DT>::to_f((uint16_t)(gsel ? bw >> 16 : bw & 0xffffu));
-                const uint32_t c2[2] = {cw.x, cw.y};
                 // The row's group takes four weight values w_q = s*q + b: their
-                // hi and lo halves as byte tables (low bytes, high bytes), so a
-                // byte permute turns two codes into two packed halves.
-                uint32_t thA = 0, thB = 0, tlA = 0, tlB = 0;
+                // hi and lo halves as byte tables (low bytes of entries 0..3,
+                // high bytes), so a byte permute turns two codes into two
+                // packed halves.
+                const float w0 = bi2, w1 = fmaf(sc, 1.f, bi2), w2 = fmaf(sc, 2.f, bi2), w3 = fmaf(sc, 3.f, bi2);
+                const uint32_t h01 = pack2<DT>(w0, w1), h23 = pack2<DT>(w2, w3);
+                const uint32_t l01 = pack2<DT>(w0 - Half<DT>::to_f((uint16_t)(h01 & 0xffffu)),
+                                               w1 - Half<DT>::to_f((uint16_t)(h01 >> 16)));
+                const uint32_t l23 = pack2<DT>(w2 - Half<DT>::to_f((uint16_t)(h23 & 0xffffu)),
+                                               w3 - Half<DT>::to_f((uint16_t)(h23 >> 16)));
+                const uint32_t thA = __byte_perm(h01, h23, 0x6420), thB = __byte_perm(h01, h23, 0x7531);
+                const uint32_t tlA = __byte_perm(l01, l23, 0x6420), tlB = __byte_perm(l01, l23, 0x7531);
+                // class order within the word's 16 codes: column 4p + j holds
+                // code 4j + p (the activations are permuted alike)
+                uint32_t hi[8], lo[8];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const float w = fmaf(sc, (float)q, bi2);
-                    const uint32_t hl = pack2<DT>(w, w - Half<DT>::to_f(Half<DT>::from_f(w)));
-                    thA |= (hl & 0xffu) << (8 * q);
-                    thB |= ((hl >> 8) & 0xffu) << (8 * q);
-                    tlA |= ((hl >> 16) & 0xffu) << (8 * q);
-                    tlB |= (hl >> 24) << (8 * q);
+                for (int p = 0; p < 4; ++p) {
+                    const uint32_t m = (cw >> (2 * p)) & 0x03030303u;  // byte j: code 4j + p
+                    const uint32_t sel = m | (m << 4) | 0x40404040u;   // nibbles (q, q + 4) per code
+                    const uint32_t sel2 = sel >> 16;
+                    hi[2 * p] = __byte_perm(thA, thB, sel);
+                    hi[2 * p + 1] = __byte_perm(thA, thB, sel2);
+                    lo[2 * p] = __byte_perm(tlA, tlB, sel);
+                    lo[2 * p + 1] = __byte_perm(tlA, tlB, sel2);
                 }
-#pragma unroll
-                for (int word = 0; word < 2; ++word) {
-                    // class order within the 16 codes of the word: column 4p + j
-                    // holds code 4j + p (the activations are permuted alike)
-                    uint32_t hi[8], lo[8];
-#pragma unroll
-                    for (int p = 0; p < 4; ++p) {
-                        const uint32_t m = (c2[word] >> (2 * p)) & 0x03030303u;  // byte j: code 4j + p
-                        const uint32_t sel = m | (m << 4) | 0x40404040u;         // nibbles (q, q + 4) per code
-                        const uint32_t sel2 = sel >> 16;
-                        hi[2 * p] = __byte_perm(thA, thB, sel);
-                        hi[2 * p + 1] = __byte_perm(thA, thB, sel2);
-                        lo[2 * p] = __byte_perm(tlA, tlB, sel);
-                        lo[2 * p + 1] = __byte_perm(tlA, tlB, sel2);
-                    }
-                    const int k0 = half * 32 + word * 16;
-                    const uint32_t o0 = sw128(ra, k0), o1 = sw128(ra, k0 + 8);
-                    *reinterpret_cast<uint4*>(sA + o0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                    *reinterpret_cast<uint4*>(sA + o1) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-                    *reinterpret_cast<uint4*>(sL + o0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                    *reinterpret_cast<uint4*>(sL + o1) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
-                }
+                const int k0 = wq * 16;
+                const uint32_t o0 = sw128(ra, k0), o1 = sw128(ra, k0 + 8);
+                *reinterpret_cast<uint4*>(sA + o0) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4*>(sA + o1) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                *reinterpret_cast<uint4*>(sL + o0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                *reinterpret_cast<uint4*>(sL + o1) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
             }
             // the next k-block's load stage has landed (this thread's copies;
             // the barrier publishes everyone's), and this k-block's A tiles are
@@ -358,14 +357,14 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
         tc_fence_after();
 
         // ---- epilogue: warp w reads TMEM lanes 32 (w & 3) + lane, columns
-        // 64 (w >> 2) + [0, 64)
+        // 32 (w >> 2) + [0, 32)
         const int r = 32 * (warp & 3) + lane;  // A row = TMEM lane
-        const int c0 = 64 * (warp >> 2);
+        const int c0 = 32 * (warp >> 2);
         if (MODE == kModeUpSwiglu) {
             float* sG = reinterpret_cast<float*>(smem);  // [token][64] gate sums (the A slots are free)
             if (r >= 64) {
 #pragma unroll 1
-                for (int cc = 0; cc < 64; cc += 16) {
+                for (int cc = 0; cc < 32; cc += 16) {
                     uint32_t v[16];
                     tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + c0 + cc, v);
 #pragma unroll
@@ -376,7 +375,7 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
             __syncthreads();
             if (r < 64) {
 #pragma unroll 1
-                for (int cc = 0; cc < 64; cc += 16) {
+                for (int cc = 0; cc < 32; cc += 16) {
                     uint32_t v[16];
                     tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + c0 + cc, v);
 #pragma unroll
@@ -390,7 +389,7 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
             }
         } else {
 #pragma unroll 1
-            for (int cc = 0; cc < 64; cc += 16) {
+            for (int cc = 0; cc < 32; cc += 16) {
                 uint32_t v[16];
                 tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + c0 + cc, v);
 #pragma unroll

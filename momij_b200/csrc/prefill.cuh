@@ -11,7 +11,7 @@
 namespace momij {
 
 constexpr int kBlockTokens = 128;  // MMA N (tokens) per tile, at most
-constexpr int kGroupedThreads = 256;
+constexpr int kGroupedThreads = 512;
 
 // Block list header (int32): [0] blocks.  Entries from +4: (expert, first
 // sorted position, pairs, 0).
