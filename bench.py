@@ -417,6 +417,8 @@ def run_gpu(args, cfg) -> None:
             traffic = json.load(open(tf)).get(args.config, {}).get("traffic_bytes_per_launch")
         except Exception:
             traffic = None
+    if tensor_roof is not None:
+        tensor_roof["traffic"] = traffic
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
