@@ -55,7 +55,7 @@ constexpr int kTmemCols = kBlockTokens;      // fp32 accumulator columns
 static_assert(kLoadBytes % 1024 == 0 && kSlotA % 1024 == 0, "stages keep the 1024-B swizzle alignment");
 static_assert(grouped_smem_bytes() == (size_t)kASlots * kSlotA + (size_t)kLoadStages * kLoadBytes + 1024,
               "host and kernel agree on the shared-memory size");
-constexpr int kMmaWaitLimit = 1 << 24;
+constexpr int kMmaWaitLimit = 1 << 22;
 
 // tcgen05 shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row
 // groups 1024 B apart (leading byte offset unused for swizzled K-major).
@@ -95,6 +95,17 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 // element 4j + p moves to 4p + j (the order the dequantised weight tiles use).
 __device__ __forceinline__ int class_order16(int c) {
     return (c & ~15) | ((c & 3) << 2) | ((c >> 2) & 3);
+}
+// Named barrier `id` over `count` threads that also ANDs a predicate.
+__device__ __forceinline__ bool bar_and(int id, int count, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n"
+        " selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
 }
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
     asm volatile(
@@ -167,14 +178,29 @@ __global__ void class_order_kernel(const uint4* __restrict__ x, uint4* __restric
     pdl_launch_dependents();
 }
 
+// Warp roles: warps [0, 16) dequantise (thread (ra, wq): 16 codes of row ra
+// per k-block) and run the epilogue; warps [16, 20) load (thread pl: token
+// pl's row segment, row pl's codes, scale and bias words); the last warp's
+// lane 0 issues the MMAs.  Hand-offs per k-block g (stage g % kLoadStages,
+// A slot g % kASlots) are mbarriers:
+//   load_full[st]   loaders -> dequant + MMA   (128 arrivals, after each
+//                   loader's copies landed and a generic->async proxy fence)
+//   a_full[as]      dequant -> MMA             (16 warp arrivals, after the fence)
+//   a_empty[as]     MMA commit -> dequant      (slot reusable)
+//   load_empty[st]  MMA commit + 16 dequant warps -> loaders (stage reusable)
+//   done            MMA commit -> epilogue      (per tile)
+//   tmem_free       16 epilogue warps -> MMA    (accumulator reusable)
+// Every wait is bounded; a timeout sets the kernel's error word and ends the
+// waiting role, whose partners then time out too.
 template <int DT, int GS, int MODE>
 __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const GroupedArgs a) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char* smem =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ uint32_t s_tmem;
-    __shared__ __align__(8) uint64_t s_bar[kASlots];  // MMA completion per A slot
-    __shared__ int s_pair[kBlockTokens], s_row[kBlockTokens];
+    __shared__ __align__(8) uint64_t bar_full[kLoadStages], bar_lempty[kLoadStages];
+    __shared__ __align__(8) uint64_t bar_afull[kASlots], bar_aempty[kASlots];
+    __shared__ __align__(8) uint64_t bar_done, bar_tmem, bar_fin;
     __shared__ int s_timeout;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
@@ -195,7 +221,17 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     if (tid == 0) {
-        for (int s = 0; s < kASlots; ++s) mbar_init(&s_bar[s], 1);
+        for (int s = 0; s < kLoadStages; ++s) {
+            mbar_init(&bar_full[s], 32 * kLoadWarps);
+            mbar_init(&bar_lempty[s], kDequantWarps + 1);
+        }
+        for (int s = 0; s < kASlots; ++s) {
+            mbar_init(&bar_afull[s], kDequantWarps);
+            mbar_init(&bar_aempty[s], 1);
+        }
+        mbar_init(&bar_done, 1);
+        mbar_init(&bar_tmem, kDequantWarps);
+        mbar_init(&bar_fin, 1);
         mbar_fence_init();
         s_timeout = 0;
     }
@@ -204,92 +240,154 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
     tc_fence_after();
     const uint32_t tmem = s_tmem;
 
-    uint32_t phase[kASlots] = {0u, 0u};
-    bool pending[kASlots] = {false, false};
-    auto wait_stage = [&](int s) {
-        bool ok = false;
-        for (int it = 0; it < kMmaWaitLimit && !ok; ++it) ok = mbar_try_wait(&s_bar[s], phase[s]);
-        if (!ok) s_timeout = 1;
-        phase[s] ^= 1u;
-        pending[s] = false;
-    };
-
     const int KB = a.Kd / 64;
     const int nsb = a.Kd / GS;
-    const int ra = tid >> 2, wq = tid & 3;  // this thread dequantises row ra, codes 16 wq + [0, 16)
     const int4* blist = reinterpret_cast<const int4*>(a.blocks + kBlockHeader);
-
-#pragma unroll 1
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
-        const int bi = t / nrb, rb = t - bi * nrb;
-        const int4 blk = blist[bi];
-        const int e = blk.x, start = blk.y, cnt = blk.z;
-        // a malformed entry (it cannot come from block_list_kernel) is an error, not an access
-        if (e < 0 || e >= a.E || start < 0 || cnt < 1 || cnt > kBlockTokens || start + cnt > a.P) {
-            if (tid == 0) atomicExch(a.status + 2, MOMIJ_ERR_WORKSPACE);
-            continue;
+    unsigned char* const ring = smem + kASlots * kSlotA;
+    // bounded wait; once any role of the CTA gave up, every later wait fails
+    // at once, so all roles wind down quickly
+    volatile int* timed_out = &s_timeout;
+    auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+        for (int it = 0; it < kMmaWaitLimit; ++it) {
+            if (mbar_try_wait(bar, parity)) return true;
+            if ((it & 1023) == 1023 && *timed_out) return false;
         }
-        const int nmma = (cnt + 15) & ~15;
-        if (tid < kBlockTokens) {
-            const int p = tid < cnt ? min(max(a.pairs[start + tid], 0), a.P - 1) : 0;
-            s_pair[tid] = p;
-            s_row[tid] = a.x_per_pair ? p : p / a.Ktop;
-        }
-        __syncthreads();  // s_row ready; the previous tile's epilogue is done with shared memory
-        unsigned char* const ring = smem + kASlots * kSlotA;
+        *timed_out = 1;
+        return false;
+    };
+    // a malformed entry (it cannot come from block_list_kernel) is an error, not an access
+    auto tile_ok = [&](const int4& blk) {
+        return !(blk.x < 0 || blk.x >= a.E || blk.y < 0 || blk.z < 1 || blk.z > kBlockTokens ||
+                 blk.y + blk.z > a.P);
+    };
+    // weight row of tile row r (0..127) of row block rb
+    auto weight_row = [&](int e, int rb, int r) -> size_t {
+        int gr;
+        if (MODE == kModeUpSwiglu) gr = (r < 64) ? rb * 64 + r : a.Ru + rb * 64 + (r - 64);
+        else gr = rb * 128 + r;
+        return (size_t)e * a.N + gr;
+    };
 
-        // k-block kb's load stage: token rows (MMA layout), the codes of the
-        // 128 rows (thread r < 128: row r) and the words holding their
-        // group's scale and bias (nsb is even, so the word is 4-B aligned)
-        auto issue_load = [&](int kb) {
-            unsigned char* st = ring + (kb % kLoadStages) * kLoadBytes;
-            for (int i = tid; i < nmma * 8; i += kGroupedThreads) {
-                const int n = i >> 3, part = i & 7;
-                const bool v = n < cnt;
-                const uint16_t* src = a.x + (size_t)(v ? s_row[n] : 0) * a.Kd + kb * 64 + part * 8;
-                cp_async16(smem_u32(st + sw128(n, part * 8)), src, v);
+    if (warp == kDequantWarps + kLoadWarps) {
+        // ---- MMA issue (one thread) ------------------------------------------
+        if (lane == 0) {
+            int g = 0, tcount = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int4 blk = blist[t / nrb];
+                if (!tile_ok(blk)) continue;
+                const int nmma = (blk.z + 15) & ~15;
+                if (tcount > 0) ok = wait(&bar_tmem, (tcount - 1) & 1);  // the epilogue has read TMEM
+                tc_fence_after();
+                const uint32_t idesc = idesc_f16<DT>(nmma);
+                for (int kb = 0; kb < KB && ok; ++kb, ++g) {
+                    const int st = g % kLoadStages, as = g % kASlots;
+                    ok = wait(&bar_afull[as], (g / kASlots) & 1) && wait(&bar_full[st], (g / kLoadStages) & 1);
+                    if (!ok) break;
+                    tc_fence_after();
+                    unsigned char* sA = smem + as * kSlotA;
+                    unsigned char* sL = sA + kStageA;
+                    unsigned char* sB = ring + st * kLoadBytes;
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t bd = sdesc_sw128(smem_u32(sB) + kk * 32);
+#pragma unroll
+                        for (int part = 0; part < 2; ++part) {  // D += A_hi B, then D += A_lo B
+                            const uint64_t ad = sdesc_sw128(smem_u32(part ? sL : sA) + kk * 32);
+                            const uint32_t accum = (kb > 0 || kk > 0 || part > 0) ? 1u : 0u;
+                            asm volatile(
+                                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                                " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+                                "l"(ad), "l"(bd), "r"(idesc), "r"(accum));
+                        }
+                    }
+                    asm volatile(
+                        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                            smem_u32(&bar_aempty[as])));
+                    asm volatile(
+                        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                            smem_u32(&bar_lempty[st])));
+                }
+                if (!ok) break;
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                    smem_u32(&bar_done)));
+                ++tcount;
             }
-            if (tid < 3 * 128) {  // thread 128 j + r: row r's codes (j = 0), scale word (1) or bias word (2)
-                const int j = tid >> 7, rr = tid & 127;
-                int gr;
-                if (MODE == kModeUpSwiglu) gr = (rr < 64) ? rb * 64 + rr : a.Ru + rb * 64 + (rr - 64);
-                else gr = rb * 128 + rr;
-                const size_t row = (size_t)e * a.N + gr;
-                if (j == 0) {
-                    cp_async16(smem_u32(st + kLoadCodes + rr * 16), a.w + row * (size_t)(a.Kd / 16) + kb * 4, true);
-                } else {
-                    const size_t gw = row * nsb + (((size_t)kb * 64 / GS) & ~(size_t)1);
-                    cp_async4(smem_u32(st + (j == 1 ? kLoadScales : kLoadBiases) + rr * 4), (j == 1 ? a.s : a.b) + gw,
-                              true);
+            // every MMA issued has completed before TMEM is released
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                smem_u32(&bar_fin)));
+            wait(&bar_fin, 0);
+        }
+    } else if (warp >= kDequantWarps) {
+        // ---- loaders ------------------------------------------------------------
+        const int pl = tid - 32 * kDequantWarps;  // 0..127
+        int g = 0, pub = 0;                       // stages issued, stages published
+        bool ok = true;
+        for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            const int bi = t / nrb, rb = t - bi * nrb;
+            const int4 blk = blist[bi];
+            if (!tile_ok(blk)) continue;
+            const int e = blk.x, start = blk.y, cnt = blk.z;
+            const int nmma = (cnt + 15) & ~15;
+            int xrow = 0;
+            if (pl < cnt) {
+                const int p = min(max(a.pairs[start + pl], 0), a.P - 1);
+                xrow = a.x_per_pair ? p : p / a.Ktop;
+            }
+            const size_t wrow = weight_row(e, rb, pl);
+            for (int kb = 0; kb < KB; ++kb, ++g) {
+                const int st = g % kLoadStages;
+                if (g >= kLoadStages && !(ok = wait(&bar_lempty[st], (g / kLoadStages - 1) & 1))) break;
+                unsigned char* sp = ring + st * kLoadBytes;
+                if (pl < nmma) {
+                    const uint16_t* src = a.x + (size_t)xrow * a.Kd + kb * 64;
+#pragma unroll
+                    for (int part = 0; part < 8; ++part)
+                        cp_async16(smem_u32(sp + sw128(pl, part * 8)), src + part * 8, pl < cnt);
+                }
+                cp_async16(smem_u32(sp + kLoadCodes + pl * 16), a.w + wrow * (size_t)(a.Kd / 16) + kb * 4, true);
+                const size_t gw = wrow * nsb + (((size_t)kb * 64 / GS) & ~(size_t)1);
+                cp_async4(smem_u32(sp + kLoadScales + pl * 4), a.s + gw, true);
+                cp_async4(smem_u32(sp + kLoadBiases + pl * 4), a.b + gw, true);
+                cp_async_commit();
+                if (g - pub >= kLoadAhead - 1) {  // stage `pub` has landed: publish it
+                    cp_async_wait<kLoadAhead - 1>();
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mbar_arrive(&bar_full[pub % kLoadStages]);
+                    ++pub;
                 }
             }
-        };
-#pragma unroll 1
-        for (int kb = 0; kb < kLoadAhead; ++kb) {
-            if (kb < KB) issue_load(kb);
-            cp_async_commit();  // one group per k-block (possibly empty)
         }
-        // k-block 0's stage has landed for every thread
-        cp_async_wait<kLoadAhead - 1>();
+        cp_async_wait<0>();
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-
-#pragma unroll 1
-        for (int kb = 0; kb < KB; ++kb) {
-            const int s = kb % kASlots;
-            // the MMAs of k-block kb - 2 used A slot s and load stage (kb + kLoadAhead) % kLoadStages
-            if (pending[s]) wait_stage(s);
-            if (kb + kLoadAhead < KB) issue_load(kb + kLoadAhead);
-            cp_async_commit();
-            unsigned char* st = ring + (kb % kLoadStages) * kLoadBytes;
-            unsigned char* sA = smem + s * kSlotA;  // hi
-            unsigned char* sL = sA + kStageA;        // lo
-            unsigned char* sB = st;
-            {
-                const uint32_t cw = *reinterpret_cast<const uint32_t*>(st + kLoadCodes + ra * 16 + wq * 4);
+        for (; pub < g; ++pub) mbar_arrive(&bar_full[pub % kLoadStages]);
+    } else {
+        // ---- dequantise + epilogue ------------------------------------------------
+        const int ra = tid >> 2, wq = tid & 3;  // row ra, codes 16 wq + [0, 16) of each k-block
+        int g = 0, tcount = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+            const int bi = t / nrb, rb = t - bi * nrb;
+            const int4 blk = blist[bi];
+            if (!tile_ok(blk)) {
+                if (tid == 0) atomicExch(a.status + 2, MOMIJ_ERR_WORKSPACE);
+                continue;
+            }
+            const int start = blk.y, cnt = blk.z;
+            // no early exit inside the tile: the 16 warps meet at named
+            // barriers below, so a failed wait only skips the work
+            for (int kb = 0; kb < KB; ++kb, ++g) {
+                const int st = g % kLoadStages, as = g % kASlots;
+                if (ok && g >= kASlots) ok = wait(&bar_aempty[as], (g / kASlots - 1) & 1);
+                if (ok) ok = wait(&bar_full[st], (g / kLoadStages) & 1);
+                if (!ok) continue;
+                const unsigned char* sp = ring + st * kLoadBytes;
+                unsigned char* sA = smem + as * kSlotA;  // hi
+                unsigned char* sL = sA + kStageA;        // lo
+                const uint32_t cw = *reinterpret_cast<const uint32_t*>(sp + kLoadCodes + ra * 16 + wq * 4);
                 const int gsel = ((kb * 64) / GS) & 1;
-                const uint32_t sw = *reinterpret_cast<const uint32_t*>(st + kLoadScales + ra * 4);
-                const uint32_t bw = *reinterpret_cast<const uint32_t*>(st + kLoadBiases + ra * 4);
+                const uint32_t sw = *reinterpret_cast<const uint32_t*>(sp + kLoadScales + ra * 4);
+                const uint32_t bw = *reinterpret_cast<const uint32_t*>(sp + kLoadBiases + ra * 4);
                 const float sc = Half<DT>::to_f((uint16_t)(gsel ? sw >> 16 : sw & 0xffffu));
                 const float bi2 = Half<DT>::to_f((uint16_t)(gsel ? bw >> 16 : bw & 0xffffu));
                 // The row's group takes four weight values w_q = s*q + b: their
@@ -323,87 +421,77 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
                 *reinterpret_cast<uint4*>(sA + o1) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
                 *reinterpret_cast<uint4*>(sL + o0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                 *reinterpret_cast<uint4*>(sL + o1) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&bar_afull[as]);
+                    mbar_arrive(&bar_lempty[st]);
+                }
             }
-            // the next k-block's load stage has landed (this thread's copies;
-            // the barrier publishes everyone's), and this k-block's A tiles are
-            // written: both become visible to the tensor core
-            cp_async_wait<kLoadAhead - 1>();
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncthreads();
-            if (tid == 0) {
-                tc_fence_after();
-                const uint32_t idesc = idesc_f16<DT>(nmma);
+            if (ok) ok = wait(&bar_done, tcount & 1);
+            ok = bar_and(1, 32 * kDequantWarps, ok);  // the same decision in every dequantising thread
+            if (!ok) break;
+            tc_fence_after();
+
+            // ---- epilogue: warp w reads TMEM lanes 32 (w & 3) + lane, columns
+            // 32 (w >> 2) + [0, 32); the A slots (all MMAs done) stage the gate sums
+            const int r = 32 * (warp & 3) + lane;  // A row = TMEM lane
+            const int c0 = 32 * (warp >> 2);
+            const uint32_t taddr = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + c0;
+            if (MODE == kModeUpSwiglu) {
+                float* sG = reinterpret_cast<float*>(smem);  // [token][64] gate sums
+                if (r >= 64) {
+#pragma unroll 1
+                    for (int cc = 0; cc < 32; cc += 16) {
+                        uint32_t v[16];
+                        tmem_ld16(taddr + cc, v);
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const uint64_t bd = sdesc_sw128(smem_u32(sB) + kk * 32);
-#pragma unroll
-                    for (int part = 0; part < 2; ++part) {  // D += A_hi B, then D += A_lo B
-                        const uint64_t ad = sdesc_sw128(smem_u32(part ? sL : sA) + kk * 32);
-                        const uint32_t accum = (kb > 0 || kk > 0 || part > 0) ? 1u : 0u;
-                        asm volatile(
-                            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-                            " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
-                            "l"(ad), "l"(bd), "r"(idesc), "r"(accum));
+                        for (int j = 0; j < 16; ++j) sG[(c0 + cc + j) * 64 + (r - 64)] = __uint_as_float(v[j]);
                     }
                 }
-                asm volatile(
-                    "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                        smem_u32(&s_bar[s])));
-            }
-            pending[s] = true;
-        }
-        for (int s = 0; s < kASlots; ++s)
-            if (pending[s]) wait_stage(s);
-        tc_fence_after();
-
-        // ---- epilogue: warp w reads TMEM lanes 32 (w & 3) + lane, columns
-        // 32 (w >> 2) + [0, 32)
-        const int r = 32 * (warp & 3) + lane;  // A row = TMEM lane
-        const int c0 = 32 * (warp >> 2);
-        if (MODE == kModeUpSwiglu) {
-            float* sG = reinterpret_cast<float*>(smem);  // [token][64] gate sums (the A slots are free)
-            if (r >= 64) {
+                bar_sync(1, 32 * kDequantWarps);
+                if (r < 64) {
 #pragma unroll 1
-                for (int cc = 0; cc < 32; cc += 16) {
-                    uint32_t v[16];
-                    tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + c0 + cc, v);
+                    for (int cc = 0; cc < 32; cc += 16) {
+                        uint32_t v[16];
+                        tmem_ld16(taddr + cc, v);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) sG[(c0 + cc + j) * 64 + (r - 64)] = __uint_as_float(v[j]);
+                        for (int j = 0; j < 16; ++j) {
+                            const int n = c0 + cc + j;
+                            if (n < cnt) {  // act columns in class order for the down GEMM
+                                const int p = min(max(__ldg(a.pairs + start + n), 0), a.P - 1);
+                                a.out[(size_t)p * a.Ru + class_order16(rb * 64 + r)] =
+                                    swiglu_staged<DT>(__uint_as_float(v[j]), sG[n * 64 + r], a.clamp);
+                            }
+                        }
+                    }
                 }
-            }
-            tc_fence_before();
-            __syncthreads();
-            if (r < 64) {
+            } else {
 #pragma unroll 1
                 for (int cc = 0; cc < 32; cc += 16) {
                     uint32_t v[16];
-                    tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + c0 + cc, v);
+                    tmem_ld16(taddr + cc, v);
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const int n = c0 + cc + j;
-                        if (n < cnt)  // act columns in class order for the down GEMM
-                            a.out[(size_t)s_pair[n] * a.Ru + class_order16(rb * 64 + r)] =
-                                swiglu_staged<DT>(__uint_as_float(v[j]), sG[n * 64 + r], a.clamp);
+                        if (n < cnt) {
+                            const int p = min(max(__ldg(a.pairs + start + n), 0), a.P - 1);
+                            a.out[(size_t)p * a.N + rb * 128 + r] = Half<DT>::from_f(__uint_as_float(v[j]));
+                        }
                     }
                 }
             }
-        } else {
-#pragma unroll 1
-            for (int cc = 0; cc < 32; cc += 16) {
-                uint32_t v[16];
-                tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + c0 + cc, v);
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int n = c0 + cc + j;
-                    if (n < cnt)
-                        a.out[(size_t)s_pair[n] * a.N + rb * 128 + r] = Half<DT>::from_f(__uint_as_float(v[j]));
-                }
-            }
+            tc_fence_before();
+            // TMEM read and the gate sums consumed before the next tile's MMAs
+            // and dequantisation reuse them
+            bar_sync(1, 32 * kDequantWarps);
+            if (lane == 0) mbar_arrive(&bar_tmem);
+            ++tcount;
         }
-        tc_fence_before();
-        __syncthreads();  // TMEM reads done before the next tile's first MMA; shared memory free
-        tc_fence_after();
     }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
     if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
     if (tid == 0 && s_timeout) atomicExch(a.status + 2, MOMIJ_ERR_TIMEOUT);
