@@ -45,15 +45,21 @@ constexpr int kStageA = 128 * 128;           // 128 weight rows x 64 elements x 
 constexpr int kSlotA = 2 * kStageA;          // A hi + A lo
 constexpr int kASlots = 2;
 constexpr int kStageB = kBlockTokens * 128;  // tokens x 64 elements x 2 B
-constexpr int kLoadCodes = kStageB;          // 128 rows x 16 B of codes
-constexpr int kLoadScales = kLoadCodes + 128 * 16;
-constexpr int kLoadBiases = kLoadScales + 128 * 4;
-constexpr int kLoadBytes = kLoadBiases + 128 * 4;  // 19456 = 19 KB (a multiple of 1024)
+constexpr int kLoadBytes = kStageB;          // a load stage holds one k-block's token rows
 constexpr int kLoadStages = 6;
 constexpr int kLoadAhead = kLoadStages - 2;  // a stage is refilled once the MMAs of two k-blocks ago are done
+// Weight chunks (4 k-blocks): the 128 rows' codes (64 B each), then their
+// scales and biases (8 B per row: the chunk's groups), two chunks in a ring.
+constexpr int kChunkKB = 4;
+constexpr int kChunkCodes = 0;
+constexpr int kChunkScales = 128 * 64;
+constexpr int kChunkBiases = kChunkScales + 128 * 8;
+constexpr int kChunkBytes = kChunkBiases + 128 * 8;  // 10 KB
+constexpr int kChunks = 2;
 constexpr int kTmemCols = kBlockTokens;      // fp32 accumulator columns
 static_assert(kLoadBytes % 1024 == 0 && kSlotA % 1024 == 0, "stages keep the 1024-B swizzle alignment");
-static_assert(grouped_smem_bytes() == (size_t)kASlots * kSlotA + (size_t)kLoadStages * kLoadBytes + 1024,
+static_assert(grouped_smem_bytes() ==
+                  (size_t)kASlots * kSlotA + (size_t)kLoadStages * kLoadBytes + (size_t)kChunks * kChunkBytes + 1024,
               "host and kernel agree on the shared-memory size");
 constexpr int kMmaWaitLimit = 1 << 22;
 
@@ -179,15 +185,19 @@ __global__ void class_order_kernel(const uint4* __restrict__ x, uint4* __restric
 }
 
 // Warp roles: warps [0, 16) dequantise (thread (ra, wq): 16 codes of row ra
-// per k-block) and run the epilogue; warps [16, 20) load (thread pl: token
-// pl's row segment, row pl's codes, scale and bias words); the last warp's
+// per k-block) and run the epilogue; warps [16, 20) load (thread pl: part
+// pl & 7 of every 16th token's row segment from token pl >> 3; every fourth
+// k-block the next chunk: 64 code bytes per row, four threads per row, and
+// row pl's scales and biases); the last warp's
 // lane 0 issues the MMAs.  Hand-offs per k-block g (stage g % kLoadStages,
 // A slot g % kASlots) are mbarriers:
 //   load_full[st]   loaders -> dequant + MMA   (128 arrivals, after each
 //                   loader's copies landed and a generic->async proxy fence)
 //   a_full[as]      dequant -> MMA             (16 warp arrivals, after the fence)
 //   a_empty[as]     MMA commit -> dequant      (slot reusable)
-//   load_empty[st]  MMA commit + 16 dequant warps -> loaders (stage reusable)
+//   load_empty[st]  MMA commit -> loaders (stage reusable)
+//   chunk_full[cs]  loaders -> dequant (the 4 k-blocks' codes, scales, biases)
+//   chunk_empty[cs] 16 dequant warps -> loaders
 //   done            MMA commit -> epilogue      (per tile)
 //   tmem_free       16 epilogue warps -> MMA    (accumulator reusable)
 // Every wait is bounded; a timeout sets the kernel's error word and ends the
@@ -200,6 +210,7 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
     __shared__ uint32_t s_tmem;
     __shared__ __align__(8) uint64_t bar_full[kLoadStages], bar_lempty[kLoadStages];
     __shared__ __align__(8) uint64_t bar_afull[kASlots], bar_aempty[kASlots];
+    __shared__ __align__(8) uint64_t bar_cfull[kChunks], bar_cempty[kChunks];
     __shared__ __align__(8) uint64_t bar_done, bar_tmem, bar_fin;
     __shared__ int s_timeout;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -223,7 +234,11 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
     if (tid == 0) {
         for (int s = 0; s < kLoadStages; ++s) {
             mbar_init(&bar_full[s], 32 * kLoadWarps);
-            mbar_init(&bar_lempty[s], kDequantWarps + 1);
+            mbar_init(&bar_lempty[s], 1);
+        }
+        for (int s = 0; s < kChunks; ++s) {
+            mbar_init(&bar_cfull[s], 32 * kLoadWarps);
+            mbar_init(&bar_cempty[s], kDequantWarps);
         }
         for (int s = 0; s < kASlots; ++s) {
             mbar_init(&bar_afull[s], kDequantWarps);
@@ -244,6 +259,7 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
     const int nsb = a.Kd / GS;
     const int4* blist = reinterpret_cast<const int4*>(a.blocks + kBlockHeader);
     unsigned char* const ring = smem + kASlots * kSlotA;
+    unsigned char* const chunks = ring + kLoadStages * kLoadBytes;
     // bounded wait; once any role of the CTA gave up, every later wait fails
     // at once, so all roles wind down quickly
     volatile int* timed_out = &s_timeout;
@@ -329,38 +345,65 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
             if (!tile_ok(blk)) continue;
             const int e = blk.x, start = blk.y, cnt = blk.z;
             const int nmma = (cnt + 15) & ~15;
-            int xrow = 0;
-            if (pl < cnt) {
-                const int p = min(max(a.pairs[start + pl], 0), a.P - 1);
-                xrow = a.x_per_pair ? p : p / a.Ktop;
+            // token rows: thread pl copies 16-B part pl & 7 of tokens 16 j + (pl >> 3),
+            // so a warp's copy covers four whole 128-B row segments
+            int xrow[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int n = 16 * j + (pl >> 3);
+                xrow[j] = 0;
+                if (n < cnt) {
+                    const int p = min(max(a.pairs[start + n], 0), a.P - 1);
+                    xrow[j] = a.x_per_pair ? p : p / a.Ktop;
+                }
             }
             const size_t wrow = weight_row(e, rb, pl);
             for (int kb = 0; kb < KB; ++kb, ++g) {
                 const int st = g % kLoadStages;
                 if (g >= kLoadStages && !(ok = wait(&bar_lempty[st], (g / kLoadStages - 1) & 1))) break;
                 unsigned char* sp = ring + st * kLoadBytes;
-                if (pl < nmma) {
-                    const uint16_t* src = a.x + (size_t)xrow * a.Kd + kb * 64;
 #pragma unroll
-                    for (int part = 0; part < 8; ++part)
-                        cp_async16(smem_u32(sp + sw128(pl, part * 8)), src + part * 8, pl < cnt);
+                for (int j = 0; j < 8; ++j) {
+                    const int n = 16 * j + (pl >> 3), part = pl & 7;
+                    if (n < nmma)
+                        cp_async16(smem_u32(sp + sw128(n, part * 8)), a.x + (size_t)xrow[j] * a.Kd + kb * 64 + part * 8,
+                                   n < cnt);
                 }
-                cp_async16(smem_u32(sp + kLoadCodes + pl * 16), a.w + wrow * (size_t)(a.Kd / 16) + kb * 4, true);
-                const size_t gw = wrow * nsb + (((size_t)kb * 64 / GS) & ~(size_t)1);
-                cp_async4(smem_u32(sp + kLoadScales + pl * 4), a.s + gw, true);
-                cp_async4(smem_u32(sp + kLoadBiases + pl * 4), a.b + gw, true);
+                if (kb % kChunkKB == 0) {  // the weight chunk of k-blocks kb .. kb + 3 (same cp.async group)
+                    const int c = g / kChunkKB, cs = c % kChunks;
+                    if (c >= kChunks && !(ok = wait(&bar_cempty[cs], (c / kChunks - 1) & 1))) break;
+                    unsigned char* cp = chunks + cs * kChunkBytes;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {  // 64 code bytes per row, four threads per row
+                        const int i = pl + 128 * j, r = i >> 2, part = i & 3;
+                        cp_async16(smem_u32(cp + kChunkCodes + r * 64 + part * 16),
+                                   a.w + weight_row(e, rb, r) * (size_t)(a.Kd / 16) + kb * 4 + part * 4, true);
+                    }
+                    const size_t gw = wrow * nsb + (size_t)kb * 64 / GS;  // the chunk's first group (4 or 2 groups)
+                    if (GS == 64) {
+                        cp_async8(smem_u32(cp + kChunkScales + pl * 8), a.s + gw, true);
+                        cp_async8(smem_u32(cp + kChunkBiases + pl * 8), a.b + gw, true);
+                    } else {
+                        cp_async4(smem_u32(cp + kChunkScales + pl * 8), a.s + gw, true);
+                        cp_async4(smem_u32(cp + kChunkBiases + pl * 8), a.b + gw, true);
+                    }
+                }
                 cp_async_commit();
-                if (g - pub >= kLoadAhead - 1) {  // stage `pub` has landed: publish it
+                if (g - pub >= kLoadAhead - 1) {  // stage `pub` (and its chunk) has landed: publish it
                     cp_async_wait<kLoadAhead - 1>();
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     mbar_arrive(&bar_full[pub % kLoadStages]);
+                    if (pub % kChunkKB == 0) mbar_arrive(&bar_cfull[(pub / kChunkKB) % kChunks]);
                     ++pub;
                 }
             }
         }
         cp_async_wait<0>();
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        for (; pub < g; ++pub) mbar_arrive(&bar_full[pub % kLoadStages]);
+        for (; pub < g; ++pub) {
+            mbar_arrive(&bar_full[pub % kLoadStages]);
+            if (pub % kChunkKB == 0) mbar_arrive(&bar_cfull[(pub / kChunkKB) % kChunks]);
+        }
     } else {
         // ---- dequantise + epilogue ------------------------------------------------
         const int ra = tid >> 2, wq = tid & 3;  // row ra, codes 16 wq + [0, 16) of each k-block
@@ -377,19 +420,17 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
             // no early exit inside the tile: the 16 warps meet at named
             // barriers below, so a failed wait only skips the work
             for (int kb = 0; kb < KB; ++kb, ++g) {
-                const int st = g % kLoadStages, as = g % kASlots;
+                const int as = g % kASlots, c = g / kChunkKB, cs = c % kChunks, kq = kb % kChunkKB;
                 if (ok && g >= kASlots) ok = wait(&bar_aempty[as], (g / kASlots - 1) & 1);
-                if (ok) ok = wait(&bar_full[st], (g / kLoadStages) & 1);
+                if (ok && kq == 0) ok = wait(&bar_cfull[cs], (c / kChunks) & 1);
                 if (!ok) continue;
-                const unsigned char* sp = ring + st * kLoadBytes;
+                const unsigned char* cp = chunks + cs * kChunkBytes;
                 unsigned char* sA = smem + as * kSlotA;  // hi
                 unsigned char* sL = sA + kStageA;        // lo
-                const uint32_t cw = *reinterpret_cast<const uint32_t*>(sp + kLoadCodes + ra * 16 + wq * 4);
-                const int gsel = ((kb * 64) / GS) & 1;
-                const uint32_t sw = *reinterpret_cast<const uint32_t*>(sp + kLoadScales + ra * 4);
-                const uint32_t bw = *reinterpret_cast<const uint32_t*>(sp + kLoadBiases + ra * 4);
-                const float sc = Half<DT>::to_f((uint16_t)(gsel ? sw >> 16 : sw & 0xffffu));
-                const float bi2 = Half<DT>::to_f((uint16_t)(gsel ? bw >> 16 : bw & 0xffffu));
+                const uint32_t cw = *reinterpret_cast<const uint32_t*>(cp + kChunkCodes + ra * 64 + kq * 16 + wq * 4);
+                const int gi = (kb * 64) / GS - ((kb - kq) * 64) / GS;  // the group within the chunk
+                const float sc = Half<DT>::to_f(*reinterpret_cast<const uint16_t*>(cp + kChunkScales + ra * 8 + gi * 2));
+                const float bi2 = Half<DT>::to_f(*reinterpret_cast<const uint16_t*>(cp + kChunkBiases + ra * 8 + gi * 2));
                 // The row's group takes four weight values w_q = s*q + b: their
                 // hi and lo halves as byte tables (low bytes of entries 0..3,
                 // high bytes), so a byte permute turns two codes into two
@@ -425,7 +466,7 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&bar_afull[as]);
-                    mbar_arrive(&bar_lempty[st]);
+                    if (kq == kChunkKB - 1) mbar_arrive(&bar_cempty[cs]);  // the chunk's codes are read
                 }
             }
             if (ok) ok = wait(&bar_done, tcount & 1);
