@@ -36,26 +36,27 @@ namespace momij {
 
 namespace {
 
-// Shared memory: a ring of kLoadStages load stages (per k-block: the token
-// rows B in the MMA layout, the 128 weight rows' codes, and the 4-byte words
-// holding their scales and biases), copied kLoadAhead k-blocks ahead with
-// cp.async, and two slots of dequantised weights (A hi, A lo) that alternate
-// between the dequantising threads and the tensor core.
+// Shared memory: a ring of load stages (per k-block: the token rows B in the
+// MMA layout), a ring of weight chunks (codes, scales and biases of four
+// k-blocks), both filled by cp.async, and two slots of dequantised weights
+// (A hi, A lo) that alternate between the dequantising threads and the
+// tensor core.
 constexpr int kStageA = 128 * 128;           // 128 weight rows x 64 elements x 2 B (one of hi / lo)
 constexpr int kSlotA = 2 * kStageA;          // A hi + A lo
 constexpr int kASlots = 2;
 constexpr int kStageB = kBlockTokens * 128;  // tokens x 64 elements x 2 B
 constexpr int kLoadBytes = kStageB;          // a load stage holds one k-block's token rows
-constexpr int kLoadStages = 6;
-constexpr int kLoadAhead = kLoadStages - 2;  // a stage is refilled once the MMAs of two k-blocks ago are done
+constexpr int kLoadStages = 5;
 // Weight chunks (4 k-blocks): the 128 rows' codes (64 B each), then their
-// scales and biases (8 B per row: the chunk's groups), two chunks in a ring.
+// scales and biases (8 B per row: the chunk's groups); a ring of four, each
+// chunk requested two chunks (eight k-blocks) before it is dequantised.
 constexpr int kChunkKB = 4;
 constexpr int kChunkCodes = 0;
 constexpr int kChunkScales = 128 * 64;
 constexpr int kChunkBiases = kChunkScales + 128 * 8;
 constexpr int kChunkBytes = kChunkBiases + 128 * 8;  // 10 KB
-constexpr int kChunks = 2;
+constexpr int kChunks = 4;
+constexpr int kChunkAhead = 2;
 constexpr int kTmemCols = kBlockTokens;      // fp32 accumulator columns
 static_assert(kLoadBytes % 1024 == 0 && kSlotA % 1024 == 0, "stages keep the 1024-B swizzle alignment");
 static_assert(grouped_smem_bytes() ==
@@ -300,6 +301,9 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
                     const int st = g % kLoadStages, as = g % kASlots;
                     ok = wait(&bar_afull[as], (g / kASlots) & 1) && wait(&bar_full[st], (g / kLoadStages) & 1);
                     if (!ok) break;
+                    // the token rows were written by other threads' cp.async
+                    // (generic proxy): order them before the tensor core reads
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     tc_fence_after();
                     unsigned char* sA = smem + as * kSlotA;
                     unsigned char* sL = sA + kStageA;
@@ -336,8 +340,11 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
         }
     } else if (warp >= kDequantWarps) {
         // ---- loaders ------------------------------------------------------------
+        // No loader thread ever waits for its own copies: each stage's and
+        // chunk's barrier gets a cp.async-tracked arrival from every loader
+        // thread (it fires once that thread's earlier copies have landed).
         const int pl = tid - 32 * kDequantWarps;  // 0..127
-        int g = 0, pub = 0;                       // stages issued, stages published
+        int g = 0, gc = 0;                        // k-blocks and chunks issued
         bool ok = true;
         for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
             const int bi = t / nrb, rb = t - bi * nrb;
@@ -345,6 +352,33 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
             if (!tile_ok(blk)) continue;
             const int e = blk.x, start = blk.y, cnt = blk.z;
             const int nmma = (cnt + 15) & ~15;
+            const int nch = KB / kChunkKB;
+            const size_t wrow = weight_row(e, rb, pl);
+            // chunk ci of this tile: k-blocks 4 ci .. 4 ci + 3
+            auto issue_chunk = [&](int ci) -> bool {
+                const int cs = gc % kChunks;
+                if (gc >= kChunks && !wait(&bar_cempty[cs], (gc / kChunks - 1) & 1)) return false;
+                unsigned char* cp = chunks + cs * kChunkBytes;
+                const int kb = ci * kChunkKB;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {  // 64 code bytes per row, four threads per row
+                    const int i = pl + 128 * j, r = i >> 2, part = i & 3;
+                    cp_async16(smem_u32(cp + kChunkCodes + r * 64 + part * 16),
+                               a.w + weight_row(e, rb, r) * (size_t)(a.Kd / 16) + kb * 4 + part * 4, true);
+                }
+                const size_t gw = wrow * nsb + (size_t)kb * 64 / GS;  // the chunk's first group (4 or 2 groups)
+                if (GS == 64) {
+                    cp_async8(smem_u32(cp + kChunkScales + pl * 8), a.s + gw, true);
+                    cp_async8(smem_u32(cp + kChunkBiases + pl * 8), a.b + gw, true);
+                } else {
+                    cp_async4(smem_u32(cp + kChunkScales + pl * 8), a.s + gw, true);
+                    cp_async4(smem_u32(cp + kChunkBiases + pl * 8), a.b + gw, true);
+                }
+                mbar_arrive_cp_async(&bar_cfull[cs]);
+                ++gc;
+                return true;
+            };
+            for (int ci = 0; ci < kChunkAhead && ci < nch && ok; ++ci) ok = issue_chunk(ci);
             // token rows: thread pl copies 16-B part pl & 7 of tokens 16 j + (pl >> 3),
             // so a warp's copy covers four whole 128-B row segments
             int xrow[8];
@@ -357,8 +391,7 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
                     xrow[j] = a.x_per_pair ? p : p / a.Ktop;
                 }
             }
-            const size_t wrow = weight_row(e, rb, pl);
-            for (int kb = 0; kb < KB; ++kb, ++g) {
+            for (int kb = 0; kb < KB && ok; ++kb, ++g) {
                 const int st = g % kLoadStages;
                 if (g >= kLoadStages && !(ok = wait(&bar_lempty[st], (g / kLoadStages - 1) & 1))) break;
                 unsigned char* sp = ring + st * kLoadBytes;
@@ -369,45 +402,16 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
                         cp_async16(smem_u32(sp + sw128(n, part * 8)), a.x + (size_t)xrow[j] * a.Kd + kb * 64 + part * 8,
                                    n < cnt);
                 }
-                if (kb % kChunkKB == 0) {  // the weight chunk of k-blocks kb .. kb + 3 (same cp.async group)
-                    const int c = g / kChunkKB, cs = c % kChunks;
-                    if (c >= kChunks && !(ok = wait(&bar_cempty[cs], (c / kChunks - 1) & 1))) break;
-                    unsigned char* cp = chunks + cs * kChunkBytes;
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {  // 64 code bytes per row, four threads per row
-                        const int i = pl + 128 * j, r = i >> 2, part = i & 3;
-                        cp_async16(smem_u32(cp + kChunkCodes + r * 64 + part * 16),
-                                   a.w + weight_row(e, rb, r) * (size_t)(a.Kd / 16) + kb * 4 + part * 4, true);
-                    }
-                    const size_t gw = wrow * nsb + (size_t)kb * 64 / GS;  // the chunk's first group (4 or 2 groups)
-                    if (GS == 64) {
-                        cp_async8(smem_u32(cp + kChunkScales + pl * 8), a.s + gw, true);
-                        cp_async8(smem_u32(cp + kChunkBiases + pl * 8), a.b + gw, true);
-                    } else {
-                        cp_async4(smem_u32(cp + kChunkScales + pl * 8), a.s + gw, true);
-                        cp_async4(smem_u32(cp + kChunkBiases + pl * 8), a.b + gw, true);
-                    }
-                }
-                cp_async_commit();
-                if (g - pub >= kLoadAhead - 1) {  // stage `pub` (and its chunk) has landed: publish it
-                    cp_async_wait<kLoadAhead - 1>();
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    mbar_arrive(&bar_full[pub % kLoadStages]);
-                    if (pub % kChunkKB == 0) mbar_arrive(&bar_cfull[(pub / kChunkKB) % kChunks]);
-                    ++pub;
-                }
+                mbar_arrive_cp_async(&bar_full[st]);
+                if (kb % kChunkKB == 0 && kb / kChunkKB + kChunkAhead < nch) ok = issue_chunk(kb / kChunkKB + kChunkAhead);
             }
         }
-        cp_async_wait<0>();
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        for (; pub < g; ++pub) {
-            mbar_arrive(&bar_full[pub % kLoadStages]);
-            if (pub % kChunkKB == 0) mbar_arrive(&bar_cfull[(pub / kChunkKB) % kChunks]);
-        }
+        cp_async_commit();
+        cp_async_wait<0>();  // no copy in flight when the CTA ends
     } else {
         // ---- dequantise + epilogue ------------------------------------------------
         const int ra = tid >> 2, wq = tid & 3;  // row ra, codes 16 wq + [0, 16) of each k-block
-        int g = 0, tcount = 0;
+        int g = 0, gc = 0, tcount = 0;  // k-blocks, chunks consumed, tiles
         bool ok = true;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
             const int bi = t / nrb, rb = t - bi * nrb;
@@ -420,9 +424,10 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
             // no early exit inside the tile: the 16 warps meet at named
             // barriers below, so a failed wait only skips the work
             for (int kb = 0; kb < KB; ++kb, ++g) {
-                const int as = g % kASlots, c = g / kChunkKB, cs = c % kChunks, kq = kb % kChunkKB;
+                const int as = g % kASlots, cs = gc % kChunks, kq = kb % kChunkKB;
                 if (ok && g >= kASlots) ok = wait(&bar_aempty[as], (g / kASlots - 1) & 1);
-                if (ok && kq == 0) ok = wait(&bar_cfull[cs], (c / kChunks) & 1);
+                if (ok && kq == 0) ok = wait(&bar_cfull[cs], (gc / kChunks) & 1);
+                if (kq == kChunkKB - 1) ++gc;
                 if (!ok) continue;
                 const unsigned char* cp = chunks + cs * kChunkBytes;
                 unsigned char* sA = smem + as * kSlotA;  // hi

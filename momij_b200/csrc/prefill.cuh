@@ -23,9 +23,9 @@ __host__ __device__ constexpr size_t block_list_ints(int P, int E) {
 }
 
 // Dynamic shared memory of grouped_gemm_kernel: two slots of dequantised
-// weights (hi + lo, 32 KB each), six 16-KB token-row stages, two 10-KB
+// weights (hi + lo, 32 KB each), five 16-KB token-row stages, four 10-KB
 // weight chunks, 1 KB of alignment.
-__host__ __device__ constexpr size_t grouped_smem_bytes() { return 2 * 32768 + 6 * 16384 + 2 * 10240 + 1024; }
+__host__ __device__ constexpr size_t grouped_smem_bytes() { return 2 * 32768 + 5 * 16384 + 4 * 10240 + 1024; }
 
 struct GroupedArgs {
     const uint16_t* x;       // activation rows [rows, Kd], 16-element blocks in class order
