@@ -48,15 +48,16 @@ constexpr int kStageB = kBlockTokens * 128;  // tokens x 64 elements x 2 B
 constexpr int kLoadBytes = kStageB;          // a load stage holds one k-block's token rows
 constexpr int kLoadStages = 5;
 // Weight chunks (4 k-blocks): the 128 rows' codes (64 B each), then their
-// scales and biases (8 B per row: the chunk's groups); a ring of four, each
-// chunk requested two chunks (eight k-blocks) before it is dequantised.
+// scales and biases (8 B per row: the chunk's groups); a ring of four.
 constexpr int kChunkKB = 4;
 constexpr int kChunkCodes = 0;
 constexpr int kChunkScales = 128 * 64;
 constexpr int kChunkBiases = kChunkScales + 128 * 8;
 constexpr int kChunkBytes = kChunkBiases + 128 * 8;  // 10 KB
 constexpr int kChunks = 4;
-constexpr int kChunkAhead = 2;
+constexpr int kRowThreads = 128;   // loader threads copying token rows (8 x 16 B each per k-block)
+constexpr int kChunkThreads = 32;  // loader threads copying weight chunks
+static_assert(kRowThreads + kChunkThreads == 32 * kLoadWarps, "the loader warps form the two streams");
 constexpr int kTmemCols = kBlockTokens;      // fp32 accumulator columns
 static_assert(kLoadBytes % 1024 == 0 && kSlotA % 1024 == 0, "stages keep the 1024-B swizzle alignment");
 static_assert(grouped_smem_bytes() ==
@@ -186,10 +187,9 @@ __global__ void class_order_kernel(const uint4* __restrict__ x, uint4* __restric
 }
 
 // Warp roles: warps [0, 16) dequantise (thread (ra, wq): 16 codes of row ra
-// per k-block) and run the epilogue; warps [16, 20) load (thread pl: part
-// pl & 7 of every 16th token's row segment from token pl >> 3; every fourth
-// k-block the next chunk: 64 code bytes per row, four threads per row, and
-// row pl's scales and biases); the last warp's
+// per k-block) and run the epilogue; warps [16, 20) copy the token rows of
+// each k-block, warp 20 the weight chunks (codes, scales, biases of four
+// k-blocks); the last warp's
 // lane 0 issues the MMAs.  Hand-offs per k-block g (stage g % kLoadStages,
 // A slot g % kASlots) are mbarriers:
 //   load_full[st]   loaders -> dequant + MMA   (128 arrivals, after each
@@ -234,11 +234,11 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
     }
     if (tid == 0) {
         for (int s = 0; s < kLoadStages; ++s) {
-            mbar_init(&bar_full[s], 32 * kLoadWarps);
+            mbar_init(&bar_full[s], kRowThreads);
             mbar_init(&bar_lempty[s], 1);
         }
         for (int s = 0; s < kChunks; ++s) {
-            mbar_init(&bar_cfull[s], 32 * kLoadWarps);
+            mbar_init(&bar_cfull[s], kChunkThreads);
             mbar_init(&bar_cempty[s], kDequantWarps);
         }
         for (int s = 0; s < kASlots; ++s) {
@@ -340,70 +340,81 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
         }
     } else if (warp >= kDequantWarps) {
         // ---- loaders ------------------------------------------------------------
-        // No loader thread ever waits for its own copies: each stage's and
-        // chunk's barrier gets a cp.async-tracked arrival from every loader
-        // thread (it fires once that thread's earlier copies have landed).
-        const int pl = tid - 32 * kDequantWarps;  // 0..127
-        int g = 0, gc = 0;                        // k-blocks and chunks issued
+        // Two streams on separate threads, so neither waits for the other's
+        // copies: warps 16-19 copy token rows (stage per k-block), warp 20
+        // weight chunks.  No loader thread waits on its own copies:
+        // every stage's / chunk's barrier gets a cp.async-tracked arrival from
+        // each thread of its stream (it fires once that thread's earlier
+        // copies have landed).
+        const int pl = tid - 32 * kDequantWarps;  // 0..159
+        const bool rows_stream = pl < kRowThreads;
+        const int ps = rows_stream ? pl : pl - kRowThreads;
+        int g = 0, gc = 0;  // k-blocks and chunks issued
         bool ok = true;
         for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
             const int bi = t / nrb, rb = t - bi * nrb;
             const int4 blk = blist[bi];
             if (!tile_ok(blk)) continue;
             const int e = blk.x, start = blk.y, cnt = blk.z;
-            const int nmma = (cnt + 15) & ~15;
-            const int nch = KB / kChunkKB;
-            const size_t wrow = weight_row(e, rb, pl);
-            // chunk ci of this tile: k-blocks 4 ci .. 4 ci + 3
-            auto issue_chunk = [&](int ci) -> bool {
-                const int cs = gc % kChunks;
-                if (gc >= kChunks && !wait(&bar_cempty[cs], (gc / kChunks - 1) & 1)) return false;
-                unsigned char* cp = chunks + cs * kChunkBytes;
-                const int kb = ci * kChunkKB;
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {  // 64 code bytes per row, four threads per row
-                    const int i = pl + 128 * j, r = i >> 2, part = i & 3;
-                    cp_async16(smem_u32(cp + kChunkCodes + r * 64 + part * 16),
-                               a.w + weight_row(e, rb, r) * (size_t)(a.Kd / 16) + kb * 4 + part * 4, true);
-                }
-                const size_t gw = wrow * nsb + (size_t)kb * 64 / GS;  // the chunk's first group (4 or 2 groups)
-                if (GS == 64) {
-                    cp_async8(smem_u32(cp + kChunkScales + pl * 8), a.s + gw, true);
-                    cp_async8(smem_u32(cp + kChunkBiases + pl * 8), a.b + gw, true);
-                } else {
-                    cp_async4(smem_u32(cp + kChunkScales + pl * 8), a.s + gw, true);
-                    cp_async4(smem_u32(cp + kChunkBiases + pl * 8), a.b + gw, true);
-                }
-                mbar_arrive_cp_async(&bar_cfull[cs]);
-                ++gc;
-                return true;
-            };
-            for (int ci = 0; ci < kChunkAhead && ci < nch && ok; ++ci) ok = issue_chunk(ci);
-            // token rows: thread pl copies 16-B part pl & 7 of tokens 16 j + (pl >> 3),
-            // so a warp's copy covers four whole 128-B row segments
-            int xrow[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int n = 16 * j + (pl >> 3);
-                xrow[j] = 0;
-                if (n < cnt) {
-                    const int p = min(max(a.pairs[start + n], 0), a.P - 1);
-                    xrow[j] = a.x_per_pair ? p : p / a.Ktop;
-                }
-            }
-            for (int kb = 0; kb < KB && ok; ++kb, ++g) {
-                const int st = g % kLoadStages;
-                if (g >= kLoadStages && !(ok = wait(&bar_lempty[st], (g / kLoadStages - 1) & 1))) break;
-                unsigned char* sp = ring + st * kLoadBytes;
+            if (rows_stream) {
+                // thread ps copies 16-B part ps & 7 of tokens 16 j + (ps >> 3),
+                // so a warp's copy covers four whole 128-B row segments; the
+                // source rows and the swizzled destinations are set per tile
+                const int nmma = (cnt + 15) & ~15, part = ps & 7;
+                const uint16_t* src[8];
+                uint32_t dst[8];
+                int nv = 0;  // copies of this thread: tokens < nmma (the first nv of j)
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    const int n = 16 * j + (pl >> 3), part = pl & 7;
-                    if (n < nmma)
-                        cp_async16(smem_u32(sp + sw128(n, part * 8)), a.x + (size_t)xrow[j] * a.Kd + kb * 64 + part * 8,
-                                   n < cnt);
+                    const int n = 16 * j + (ps >> 3);
+                    int xr = 0;
+                    if (n < cnt) {
+                        const int p = min(max(a.pairs[start + n], 0), a.P - 1);
+                        xr = a.x_per_pair ? p : p / a.Ktop;
+                    }
+                    src[j] = a.x + (size_t)xr * a.Kd + part * 8;
+                    dst[j] = sw128(n, part * 8) | (n < cnt ? 0u : 0x80000000u);  // top bit: zero-fill
+                    nv += n < nmma;
                 }
-                mbar_arrive_cp_async(&bar_full[st]);
-                if (kb % kChunkKB == 0 && kb / kChunkKB + kChunkAhead < nch) ok = issue_chunk(kb / kChunkKB + kChunkAhead);
+                for (int kb = 0; kb < KB && ok; ++kb, ++g) {
+                    const int st = g % kLoadStages;
+                    if (g >= kLoadStages && !(ok = wait(&bar_lempty[st], (g / kLoadStages - 1) & 1))) break;
+                    const uint32_t sp = smem_u32(ring + st * kLoadBytes);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (j < nv)
+                            cp_async16(sp + (dst[j] & 0x7fffffffu), src[j] + kb * 64, !(dst[j] >> 31));
+                    mbar_arrive_cp_async(&bar_full[st]);
+                }
+            } else {
+                // chunk ci: k-blocks 4 ci .. 4 ci + 3; codes 64 B per row (four
+                // threads per row), then the rows' scale and bias words
+                const int nch = KB / kChunkKB;
+                for (int ci = 0; ci < nch && ok; ++ci, ++gc) {
+                    const int cs = gc % kChunks;
+                    if (gc >= kChunks && !(ok = wait(&bar_cempty[cs], (gc / kChunks - 1) & 1))) break;
+                    unsigned char* cp = chunks + cs * kChunkBytes;
+                    const int kb = ci * kChunkKB;
+#pragma unroll 4
+                    for (int j = 0; j < 16; ++j) {
+                        const int i = ps + 32 * j, r = i >> 2, pt = i & 3;
+                        cp_async16(smem_u32(cp + kChunkCodes + r * 64 + pt * 16),
+                                   a.w + weight_row(e, rb, r) * (size_t)(a.Kd / 16) + kb * 4 + pt * 4, true);
+                    }
+#pragma unroll 4
+                    for (int h = 0; h < 4; ++h) {
+                        const int r = ps + 32 * h;
+                        const size_t gw = weight_row(e, rb, r) * nsb + (size_t)kb * 64 / GS;  // first group of the chunk
+                        if (GS == 64) {
+                            cp_async8(smem_u32(cp + kChunkScales + r * 8), a.s + gw, true);
+                            cp_async8(smem_u32(cp + kChunkBiases + r * 8), a.b + gw, true);
+                        } else {
+                            cp_async4(smem_u32(cp + kChunkScales + r * 8), a.s + gw, true);
+                            cp_async4(smem_u32(cp + kChunkBiases + r * 8), a.b + gw, true);
+                        }
+                    }
+                    mbar_arrive_cp_async(&bar_cfull[cs]);
+                }
             }
         }
         cp_async_commit();

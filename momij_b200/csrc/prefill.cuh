@@ -12,7 +12,7 @@ namespace momij {
 
 constexpr int kBlockTokens = 128;  // MMA N (tokens) per tile, at most
 constexpr int kDequantWarps = 16;  // dequantise + epilogue
-constexpr int kLoadWarps = 4;      // cp.async producers
+constexpr int kLoadWarps = 5;      // cp.async producers (4 token-row warps, 1 weight-chunk warp)
 constexpr int kGroupedThreads = 32 * (kDequantWarps + kLoadWarps + 1);  // + one MMA-issuing warp
 
 // Block list header (int32): [0] blocks.  Entries from +4: (expert, first
