@@ -14,7 +14,9 @@
 //     2^-22 of it -- below the fp32 rounding of the reference's accumulator);
 //   * mma.sync m16n8k32 u8 x s8 -> s32 accumulates the four classes with a
 //     Horner shift (D <<= 2 between classes), so each digit plane's dot
-//     product is exact;
+//     product is exact (units of several tokens shift the operand instead,
+//     (w >> 2p) & 0x03030303, once for all their tokens, and scale the
+//     result by 64 exactly);
 //   * the N dimension of the MMA separates digit groups and digit planes:
 //     an MMA's K slab holds the codes of two digit groups, and its 8 columns
 //     are (group, digit 0|1|2|unused), so one MMA per class and K half gives
@@ -219,6 +221,7 @@ struct GemvPhase {
     static constexpr int DIST = STAGES - 1;  // items in flight ahead of the one computed
     static constexpr int SPC = 256 / GS;     // scale groups per row of a chunk
     static constexpr int SLOT = slot_bytes(TMAX);
+    static constexpr bool kHorner = (TMAX == 1);  // class weights evened on the accumulators
 
     // Position in the warp's item sequence: tile and chunk pair.
     struct Iter {
@@ -443,19 +446,25 @@ struct GemvPhase {
 
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
-            if (p) {
+            // One token: class p enters as q*4^p (one AND) and a Horner shift
+            // of the accumulators between classes evens the weights out.
+            // Several tokens: the shift moves to the operand (q itself, one
+            // shift + AND per word, shared by the tokens) instead of being
+            // paid on every token's accumulators; D is then 64x smaller,
+            // which the epilogue restores exactly.
+            if (kHorner && p) {
 #pragma unroll
-                for (int j = 0; j < TMAX; ++j)
+                for (int h = 0; h < 2; ++h)
 #pragma unroll
-                    for (int h = 0; h < 2; ++h)
-#pragma unroll
-                        for (int r = 0; r < 4; ++r) D[j][h][r] <<= 2;
+                    for (int r = 0; r < 4; ++r) D[0][h][r] <<= 2;
             }
             const uint32_t mask = 0x03030303u << (2 * p);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                const uint32_t a0 = wa[h].x & mask, a1 = wb[h].x & mask;
-                const uint32_t a2 = wa[h].y & mask, a3 = wb[h].y & mask;
+                const uint32_t a0 = kHorner ? (wa[h].x & mask) : ((wa[h].x >> (2 * p)) & 0x03030303u);
+                const uint32_t a1 = kHorner ? (wb[h].x & mask) : ((wb[h].x >> (2 * p)) & 0x03030303u);
+                const uint32_t a2 = kHorner ? (wa[h].y & mask) : ((wa[h].y >> (2 * p)) & 0x03030303u);
+                const uint32_t a3 = kHorner ? (wb[h].y & mask) : ((wb[h].y >> (2 * p)) & 0x03030303u);
 #pragma unroll
                 for (int j = 0; j < TMAX; ++j) {
                     if (j < nT) {
@@ -501,7 +510,8 @@ struct GemvPhase {
                     const int d0 = odd ? s1 : cacc[0];
                     const int d1 = odd ? s2 : cacc[1];
                     const int d2 = odd ? cacc[2] : s1;
-                    const float v = fmaf((float)d0, 65536.f, fmaf((float)d1, 256.f, (float)d2));
+                    float v = fmaf((float)d0, 65536.f, fmaf((float)d1, 256.f, (float)d2));
+                    if (!kHorner) v *= 64.f;  // the Horner chain's 4^3, exactly (a power of two)
                     const float F = h ? fsv.z : fsv.x, S = h ? fsv.w : fsv.y;
                     part[h] = fmaf(sc[h], v * F, bi[h] * S);
                 }
