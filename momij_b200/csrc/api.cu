@@ -310,9 +310,9 @@ int run_fused_layer(LayerArgs a, int dtype, int gs, const Workspace& ws, cudaStr
         const size_t ring = (size_t)kConsumerWarps * stages * slot_bytes(tmax);
         if (off + ring + 256 > limit) return kNotApplicable;
         const size_t avail = limit - off - ring - 256;
-        const size_t rpt_up = 4 * (size_t)((a.nK_up + 1) / 2) * tmax * 16,
-                     rpt_dn = 4 * (size_t)((a.nK_dn + 1) / 2) * tmax * 16;  // red_floats_per_tile
-        const size_t spt_up = sb_bytes_per_tile(a.H, gs), spt_dn = sb_bytes_per_tile(a.I, gs);
+        const size_t rpt_up = 4 * (size_t)((a.nK_up + 1) / 2) * tmax * red_row(tmax),
+                     rpt_dn = 4 * (size_t)((a.nK_dn + 1) / 2) * tmax * red_row(tmax);  // red_floats_per_tile
+        const size_t spt_up = sb_bytes_per_tile(a.H, gs, tmax == 1), spt_dn = sb_bytes_per_tile(a.I, gs, tmax == 1);
         size_t bu = (size_t)(mt_up + rt - 1) / rt * rt, bd = (size_t)(mt_dn + rt - 1) / rt * rt;
         auto need = [&]() {
             return std::max(bu * rpt_up, bd * rpt_dn) + std::max(bu * spt_up, bd * spt_dn) + 16;
@@ -422,7 +422,7 @@ bool configure_gemv(GemvLaunch& L, int mode, int tmax, int gs) {
     L.grid = (int)G;
     const int nDG = a.Kd / kDigitGroup;
     const size_t limit = (size_t)max_dyn_smem();
-    const size_t pt = 4 * (size_t)((nK + 1) / 2) * tmax * 16;  // red_floats_per_tile
+    const size_t pt = 4 * (size_t)((nK + 1) / 2) * tmax * red_row(tmax);  // red_floats_per_tile
     // A CTA's slice starts as its share of the worst case; when the slice's
     // tables and token digits do not fit, slices shrink and each CTA loops
     // over several (large batches of few tokens per expert).
@@ -459,7 +459,7 @@ bool configure_gemv_smem(GemvLaunch& L, int nDG, size_t limit, size_t pt, int gs
         // all tiles at once
         const size_t ring = (size_t)kConsumerWarps * stages * slot_bytes(tmax);
         if (off + ring + 256 > limit) continue;
-        const size_t spt = sb_bytes_per_tile(a.Kd, gs);
+        const size_t spt = sb_bytes_per_tile(a.Kd, gs, true);
         const size_t bt = std::min((size_t)(a.max_tiles + rt - 1) / rt * rt,
                                    (limit - off - ring - 256) / (pt + spt) / rt * rt);
         if (bt < (size_t)rt) continue;

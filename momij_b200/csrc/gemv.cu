@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         PhaseWeights wts{a.w, a.s, a.b, a.N, a.rows_per_unit, a.Kd};
         GemvPhase<DT, GS, MODE, TMAX, STAGES> ph(tabs, wts, s_stage, 0, a.nK,
                                                  reinterpret_cast<uint16_t*>(smem + a.off_sb), a.batch_tiles,
-                                                 &s_sbar);
+                                                 &s_sbar, true);
         ph.sb_par = sb_par;
         auto ahead = [&]() { ph.load_next(); };
         if (s_ntiles > 0) ph.issue_sb(0, min(s_ntiles, a.batch_tiles));

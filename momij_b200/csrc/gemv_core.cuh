@@ -151,13 +151,33 @@ constexpr int kItemChunks = 2;
 __host__ __device__ constexpr int slot_bytes(int) { return 16 * 128; }
 // Scale/bias buffer of an epilogue batch: scales [tiles * 16][Kd/gs] then
 // biases (halves); MMA row r of the batch's tile k at row 16 k + r.
-__host__ __device__ constexpr int sb_bytes_per_tile(int Kd, int gs) { return 16 * (Kd / gs) * 2 * 2; }
+// Row stride (halves) of the scale/bias buffer: the epilogue's lanes read
+// one column of 16 rows at once, so rows are padded to a word count that
+// spreads them over the banks (= 4 mod 8 words with 16-B rows, so rows r and
+// r + 8 share a bank at most; an odd word count with 4-B rows).  With 16-B
+// rows nsb % 8 == 0, so nsb / 2 words is 0 or 4 mod 8.
+__host__ __device__ constexpr int sb_row_halves(int nsb, bool rows16) {
+    return rows16 ? 2 * ((nsb / 2) % 8 == 4 ? nsb / 2 : nsb / 2 + 4) : 2 * (((nsb + 1) / 2) | 1);
+}
+// pad: rows padded by sb_row_halves (at most 8 halves more).  The fused
+// layer kernel pads only for one-token units: with several tokens its shared
+// memory is tight and smaller epilogue batches measured worse than the bank
+// conflicts.
+__host__ __device__ constexpr int sb_bytes_per_tile(int Kd, int gs, bool pad) {
+    return 16 * (Kd / gs + (pad ? 8 : 0)) * 2 * 2;
+}
 
 // Red-buffer floats per tile: [chunk pairs][TMAX][16 rows], each the sum of
 // one item's two chunks (chunk 2cp, then + chunk 2cp + 1), a chunk's value
 // being ((G0 + G1) + (G2 + G3)) over its four digit groups.
+// A red-buffer row (16 MMA rows of one chunk pair and token slot) takes
+// red_row(TMAX) floats.  With one token the padding to 20 spreads the 8 lanes
+// that sum one output over 8 chunk pairs across distinct banks; units of
+// several tokens keep 16 (their larger buffers would cost epilogue batch
+// size, which measured worse than the conflicts).
+__host__ __device__ constexpr int red_row(int tmax) { return tmax == 1 ? 20 : 16; }
 template <int TMAX>
-__host__ __device__ constexpr int red_floats_per_tile(int nK) { return ((nK + 1) / 2) * TMAX * 16; }
+__host__ __device__ constexpr int red_floats_per_tile(int nK) { return ((nK + 1) / 2) * TMAX * red_row(TMAX); }
 // Sum of the partials of MMA row r (0..15) of token slot j of one tile over
 // its n entries (chunk pairs), computed by L lanes (an aligned group; L = 1, 2, 4 or 8; lane
 // `sub` of the group).  The association is fixed whatever L is:
@@ -170,7 +190,7 @@ __device__ __forceinline__ float tile_sum(const float* red, int n, int j, int r,
 #pragma unroll
     for (int v = 0; v < V; ++v) {
         float acc = 0.f;
-        for (int cc = sub * V + v; cc < n; cc += 8) acc += red[(cc * TMAX + j) * 16 + r];
+        for (int cc = sub * V + v; cc < n; cc += 8) acc += red[(cc * TMAX + j) * red_row(TMAX) + r];
         part[v] = acc;
     }
 #pragma unroll
@@ -243,17 +263,19 @@ struct GemvPhase {
     uint64_t* sbar; // mbarrier of the batch's scale/bias copies
     int sb_par;     // its phase parity
     bool sb16;      // scale/bias rows and tensors 16-B aligned (16-B copies, else 4-B)
+    int nsbp;       // row stride of the scale/bias buffer in halves (sb_row_halves)
 
     // ring_base: the block's rings (kConsumerWarps x STAGES x SLOT);
     // q0_: items this warp streamed through its ring in earlier phases;
     // sb_, sb_tiles_: the scale/bias buffer (batch size in tiles); sbar_: an
     // mbarrier initialised by sb_init.
     __device__ GemvPhase(const PhaseTables& tabs, const PhaseWeights& wts, unsigned char* ring_base,
-                         int q0_, int nK_, uint16_t* sb_, int sb_tiles_, uint64_t* sbar_)
+                         int q0_, int nK_, uint16_t* sb_, int sb_tiles_, uint64_t* sbar_, bool pad_sb)
         : T(tabs), W(wts), q0(q0_), nK(nK_), sb(sb_), sb_tiles(sb_tiles_), sbar(sbar_), sb_par(0) {
         const int nsb = W.Kd / GS;
         sb16 = (nsb * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(W.s) % 16) == 0 &&
                (reinterpret_cast<uintptr_t>(W.b) % 16) == 0 && (reinterpret_cast<uintptr_t>(sb) % 16) == 0;
+        nsbp = pad_sb ? sb_row_halves(nsb, sb16) : nsb;
         per_tile = red_floats_per_tile<TMAX>(nK_);
         warp = threadIdx.x >> 5;
         lane = threadIdx.x & 31;
@@ -352,14 +374,14 @@ struct GemvPhase {
             const uint16_t* gsrc = tensor ? W.b : W.s;
             const size_t goff = ((size_t)part * W.Ru + ri) * nsb;
             const uint32_t dst0 =
-                smem_u32(sb + ((size_t)tensor * sb_tiles * 16 + r) * nsb) + pc * psz;
+                smem_u32(sb + ((size_t)tensor * sb_tiles * 16 + r) * nsbp) + pc * psz;
             for (int k = tb0; k < tb1; ++k) {
                 const int4 tile = T.tiles[k];
                 if (ri >= tile.z) continue;
                 const size_t grow = (size_t)T.units[tile.x].x * W.N + tile.y;
                 const unsigned char* src =
                     reinterpret_cast<const unsigned char*>(gsrc + grow * nsb + goff) + pc * psz;
-                const uint32_t dst = dst0 + (uint32_t)((k - tb0) * 16 * nsb * 2);
+                const uint32_t dst = dst0 + (uint32_t)((k - tb0) * 16 * nsbp * 2);
                 if (sb16) cp_async16(dst, src, true);
                 else cp_async4(dst, src, true);
             }
@@ -482,10 +504,10 @@ struct GemvPhase {
         const int srow = (tau - tfirst) * 16 + (odd ? g + 8 : g);  // the lane's row in the batch
         const int nsb = W.Kd / GS;
         const uint16_t* sb_s = sb;
-        const uint16_t* sb_b = sb + (size_t)sb_tiles * 16 * nsb;
+        const uint16_t* sb_b = sb + (size_t)sb_tiles * 16 * nsbp;
         float sc[2], bi[2];
         if (SPC == 4) {  // two adjacent groups' halves in one 4-byte load
-            const int si = srow * nsb + 4 * c + 2 * (t >> 1);
+            const int si = srow * nsbp + 4 * c + 2 * (t >> 1);
             const uint32_t sv = *reinterpret_cast<const uint32_t*>(sb_s + si);
             const uint32_t bv = *reinterpret_cast<const uint32_t*>(sb_b + si);
             sc[0] = Half<DT>::to_f((uint16_t)(sv & 0xffffu));
@@ -493,7 +515,7 @@ struct GemvPhase {
             bi[0] = Half<DT>::to_f((uint16_t)(bv & 0xffffu));
             bi[1] = Half<DT>::to_f((uint16_t)(bv >> 16));
         } else {  // gs = 128: both groups share one scale
-            const int si = srow * nsb + SPC * c + (t >> 1);
+            const int si = srow * nsbp + SPC * c + (t >> 1);
             sc[0] = sc[1] = Half<DT>::to_f(sb_s[si]);
             bi[0] = bi[1] = Half<DT>::to_f(sb_b[si]);
         }
@@ -564,7 +586,7 @@ struct GemvPhase {
                 if (t < 2) {
 #pragma unroll
                     for (int j = 0; j < TMAX; ++j)
-                        if (j < nT) red_tile[(ci.cp * TMAX + j) * 16 + t * 8 + g] = acc[j];
+                        if (j < nT) red_tile[(ci.cp * TMAX + j) * red_row(TMAX) + t * 8 + g] = acc[j];
                 }
                 __syncwarp();
                 advance(ci);

@@ -146,11 +146,25 @@ __device__ void route_topk_ranks(const float* s_logits, int M, int E, int K, int
             e = c - m * E;
             const float* lg = s_logits + m * E;
             const uint32_t o = logit_order(lg[e]);
-            const int j0 = sub * per;
-            for (int j = j0; j < j0 + per; ++j) {
-                const uint32_t oj = logit_order(lg[j]);
-                greater += (oj > o) | ((oj == o) & (j < e));
+            // part `sub` compares logits sub, sub + parts, ...: the parts of a
+            // candidate read neighbouring words (no bank conflicts); four
+            // independent counts keep the loads in flight
+            int gq[4] = {0, 0, 0, 0};
+            int i = 0;
+            for (; i + 4 <= per; i += 4) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int j = sub + parts * (i + u);
+                    const uint32_t oj = logit_order(lg[j]);
+                    gq[u] += (oj > o) | ((oj == o) & (j < e));
+                }
             }
+            for (; i < per; ++i) {
+                const int j = sub + parts * i;
+                const uint32_t oj = logit_order(lg[j]);
+                gq[0] += (oj > o) | ((oj == o) & (j < e));
+            }
+            greater = (gq[0] + gq[1]) + (gq[2] + gq[3]);
         }
         for (int o = 1; o < parts; o <<= 1) greater += __shfl_xor_sync(0xffffffffu, greater, o);
         if (c < ncand && sub == 0 && greater < K) s_inds[m * K + greater] = e;
@@ -373,10 +387,10 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
     sb_init(&s_sbar_dn);
     const PhaseTables up_tabs{up_tb.tiles, up_tb.lunits, up_tb.uslot, s_cnt_up[0]};
     GemvPhase<DT, GS, kModeUpSwiglu, TMAX, STAGES> up(up_tabs, up_w, s_ring, 0, a.nK_up, s_sb, a.batch_up,
-                                                      &s_sbar_up);
+                                                      &s_sbar_up, TMAX == 1);
     const PhaseTables dn_tabs{dn_tb.tiles, dn_tb.lunits, dn_tb.uslot, s_cnt_dn[0]};
     GemvPhase<DT, GS, kModeRows, TMAX, STAGES> dn(dn_tabs, dn_w, s_ring, up.count, a.nK_dn, s_sb, a.batch_dn,
-                                                  &s_sbar_dn);
+                                                  &s_sbar_dn, TMAX == 1);
 
     // One item sequence per warp: its up items, then its down items, which
     // start streaming during the up phase's last items.
