@@ -632,7 +632,12 @@ def run_ep(args, cfg) -> None:
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": (achieved / peak) if achieved else None, "traffic": None,
                          "peak_source": peak_kind, "bytes_per_launch": up_bytes,
-                         "avg_launch_us": {"up": _us(up_ms), "down": _us(dn_ms)}},
+                         "avg_launch_us": {"up": _us(up_ms), "down": _us(dn_ms),
+                                           "plan": _us(kt[moe.KERNEL_PLAN][0] / max(kt[moe.KERNEL_PLAN][1], 1)),
+                                           "combine": _us(kt[moe.KERNEL_COMBINE][0]
+                                                          / max(kt[moe.KERNEL_COMBINE][1], 1)),
+                                           "layer": _us(kt[moe.KERNEL_LAYER][0] / max(kt[moe.KERNEL_LAYER][1], 1))}},
+            "launches_per_layer": {str(k): v[1] / L for k, v in kt.items()},
             "clocks": clocks,
             "e2e": {"value": e2e_tok_s, "unit": "tokens/s", "h2d_bytes_per_step": x_pin.numel() * 2
                     + lg_pin.numel() * 4, "d2h_bytes_per_step": y_pin.numel() * 2,

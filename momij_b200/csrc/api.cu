@@ -970,8 +970,18 @@ int momij_moe_forward(const float* logits, const void* x, const uint32_t* w_ug, 
     if (frc != kNotApplicable) return frc;
     const int tmax = tmax_for(M, Ktop, 0);
     const int slot = prof_begin(MOMIJ_KERNEL_PLAN, st);
-    int rc = cuda_status(launch(route_plan_kernel, dim3(1), dim3(1024), 0, st, logits, M, E, Ktop,
-                                tmax, ind_out, sc_out, ws.plan));
+    int rc;
+    if (M <= 32) {  // one block routes every token (a warp each) and plans
+        rc = cuda_status(launch(route_plan_kernel, dim3(1), dim3(1024), 0, st, logits, M, E, Ktop, tmax,
+                                ind_out, sc_out, ws.plan));
+    } else {  // many tokens: route on as many blocks as needed, then plan
+        const int warps = 8;
+        rc = cuda_status(launch(route_kernel, dim3((M + warps - 1) / warps), dim3(32 * warps), 0, st, logits, M,
+                                E, Ktop, ind_out, sc_out));
+        if (!rc)
+            rc = cuda_status(launch(plan_kernel, dim3(1), dim3(1024), 0, st, static_cast<const int32_t*>(ind_out),
+                                    M * Ktop, E, tmax, ws.plan, 0));
+    }
     prof_end(slot, st);
     if (rc) return rc;
     return ffn_after_plan(x, w_ug, s_ug, b_ug, w_dn, s_dn, b_dn, sc_out, y, resid_h, M, H, I, E,

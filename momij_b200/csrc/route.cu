@@ -28,12 +28,82 @@ __global__ void route_kernel(const float* __restrict__ logits, int M, int E, int
 // Runs as one block of 1024 threads; P <= MOMIJ_MAX_PAIRS.  allow_pad: an
 // index of -1 marks an empty slot (expert-parallel receive buffers): it joins
 // no unit, so its output row is left untouched.
+constexpr int kPlanCountE = 1024;  // experts up to which the plan is a counting sort
+
+// The plan by counting (E <= kPlanCountE): per-expert counts, their scans
+// (sorted offsets, empty slots first; unit offsets), then warp w places the
+// pairs of experts w, w + 32, ... in pair order with ballots and writes their
+// units.  Same plan as the rank version below, in O(E * P / 32) per warp
+// instead of O(P) per pair.
+__device__ void plan_by_counts(const int* s_e, int P, int E, int tmax, int32_t* __restrict__ plan,
+                               int* s_cnt, int* s_off, int* s_uoff, int* s_total) {
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
+    int32_t* units = plan + kPlanHeader;
+    int32_t* sorted = plan + kPlanHeader + 4 * P;
+    for (int e = tid; e <= E; e += nt) s_cnt[e] = 0;  // [E]: empty slots
+    __syncthreads();
+    for (int i = tid; i < P; i += nt) {
+        const int e = s_e[i];
+        atomicAdd(&s_cnt[e < 0 ? E : e], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int cpos = s_cnt[E], cu = 0;  // empty slots sort first
+        for (int base = 0; base < E; base += 32) {
+            const int e = base + lane;
+            const int c = e < E ? s_cnt[e] : 0, nu = (c + tmax - 1) / tmax;
+            int ic = c, iu = nu;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int yc = __shfl_up_sync(0xffffffffu, ic, o), yu = __shfl_up_sync(0xffffffffu, iu, o);
+                if (lane >= o) {
+                    ic += yc;
+                    iu += yu;
+                }
+            }
+            if (e < E) {
+                s_off[e] = cpos + ic - c;
+                s_uoff[e] = cu + iu - nu;
+            }
+            cpos += __shfl_sync(0xffffffffu, ic, 31);
+            cu += __shfl_sync(0xffffffffu, iu, 31);
+        }
+        if (lane == 0) *s_total = cu;
+    }
+    __syncthreads();
+    const unsigned below = (1u << lane) - 1u;
+    for (int e = warp; e <= E; e += nw) {  // e == E: the empty slots (index -1), at the front
+        const int c = s_cnt[e];
+        if (c == 0) continue;
+        const int key = e == E ? -1 : e, start = e == E ? 0 : s_off[e];
+        int pos = start;
+        for (int base = 0; base < P && pos - start < c; base += 32) {
+            const int i = base + lane;
+            const bool hit = i < P && s_e[i] == key;
+            const unsigned m = __ballot_sync(0xffffffffu, hit);
+            if (hit) sorted[pos + __popc(m & below)] = i;
+            pos += __popc(m);
+        }
+        if (e < E)
+            for (int k = lane; k * tmax < c; k += 32)
+                reinterpret_cast<int4*>(units)[s_uoff[e] + k] =
+                    make_int4(e, start + k * tmax, min(tmax, c - k * tmax), 0);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        plan[0] = *s_total;
+        plan[1] = MOMIJ_OK;
+        plan[2] = 0;
+    }
+}
+
 __device__ void build_plan_block(const int32_t* __restrict__ inds, int P, int E, int tmax,
                                  int32_t* __restrict__ plan, int allow_pad) {
     __shared__ int s_e[MOMIJ_MAX_PAIRS];
     __shared__ int s_flag[MOMIJ_MAX_PAIRS];
     __shared__ int s_warp[32];
     __shared__ int s_bad;
+    __shared__ int s_cnt[kPlanCountE + 1], s_off[kPlanCountE], s_uoff[kPlanCountE], s_total;
     const int tid = threadIdx.x, nt = blockDim.x;
     if (tid == 0) s_bad = 0;
     __syncthreads();
@@ -45,6 +115,10 @@ __device__ void build_plan_block(const int32_t* __restrict__ inds, int P, int E,
     __syncthreads();
     if (s_bad) {
         if (tid == 0) { plan[0] = 0; plan[1] = MOMIJ_ERR_EXPERT_INDEX; plan[2] = 0; }
+        return;
+    }
+    if (E <= kPlanCountE) {
+        plan_by_counts(s_e, P, E, tmax, plan, s_cnt, s_off, s_uoff, &s_total);
         return;
     }
     int32_t* units = plan + kPlanHeader;
