@@ -5,13 +5,14 @@ return the expert outputs, then the score-weighted combine in k order.
 
 Per layer, on every rank (M tokens of its own, K slots each):
   route -> dispatch (momij_moe_ep_dispatch: fixed-capacity rows per
-  destination, deterministic slots) -> all_to_all(rows, meta) -> local experts
+  destination, deterministic slots; the destination's expert indices ride in
+  one extra row of its segment) -> all_to_all(rows) -> local experts
   (momij_moe_gqmm2_up_swiglu + momij_moe_gqmm2 over the received rows; empty
   rows carry expert -1 and are skipped) -> all_to_all(outputs) -> combine
   (momij_moe_ep_combine into the residual stream).
 
-The buffers hold `capacity = M*K` rows per destination, so no rank ever
-needs the counts on the host (no device-to-host synchronisation per layer);
+The buffers hold `capacity = M*K` pair rows (+ the index row) per
+destination, so no rank ever needs the counts on the host (no device-to-host synchronisation per layer);
 the exchanges are all_to_all_single with equal splits over NCCL (NVLink).
 The result has the same bits as the single-GPU path on the same tokens: each
 pair's expert output is computed with the same kernel and the combine sums in
@@ -70,8 +71,14 @@ class ExpertParallelMoE:
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         if E % self.world:
             raise ValueError("experts must split evenly over the ranks")
+        # per destination: M*K pair rows (a rank's pairs may all go to one
+        # owner) + one row whose first words carry the rows' local expert
+        # indices, so one all-to-all moves rows and indices together
         self.capacity = M * K
-        rows = self.world * self.capacity
+        self.seg = self.capacity + 1
+        if self.seg > H // 2:
+            raise ValueError("the index row needs M*K + 1 <= H / 2")
+        rows = self.world * self.seg
         dev = device if device is not None else torch.device("cpu")
         self.inds = torch.empty(M, K, dtype=torch.int32, device=dev)
         self.scores = torch.empty(M, K, dtype=torch.float32, device=dev)
@@ -102,9 +109,14 @@ class ExpertParallelMoE:
         o = self.ops
         o.route(logits, self.K, self.inds, self.scores)
         o.dispatch(self.inds, h, self.send_x, self.send_meta, self.slot_map, self.status, E=self.E,
-                   world=self.world, capacity=self.capacity)
-        self._exchange(self.recv_meta, self.send_meta)
-        self._exchange(self.recv_x, self.send_x)
+                   world=self.world, capacity=self.seg)
+        if self.world > 1:
+            w, c = self.world, self.capacity
+            sx = self.send_x.view(torch.int32).view(w, self.seg, -1)
+            sx[:, c, :self.seg].copy_(self.send_meta.view(w, self.seg))  # slot c itself is empty (-1)
+            self._exchange(self.recv_x, self.send_x)
+            rx = self.recv_x.view(torch.int32).view(w, self.seg, -1)
+            self.recv_meta.view(w, self.seg).copy_(rx[:, c, :self.seg])
         o.experts(self.recv_x, self.recv_meta, self.act, self.down)
         self._exchange(self.back, self.down)
         o.combine(self.back, self.scores, self.slot_map, self.status, h)
