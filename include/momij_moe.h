@@ -67,6 +67,23 @@ int momij_version(void);
 /* Number of streaming multiprocessors of the current device, or -1. */
 int momij_device_sm_count(void);
 
+/* Stop flag: a device int32 (or NULL to clear) that every kernel of this
+ * library reads when it starts; a non-zero value makes the call skip its work
+ * and report MOMIJ_ERR_STOPPED through momij_moe_synchronize (outputs are then
+ * undefined).  Process-wide, like the reference's single stop buffer; set it
+ * before the calls it should affect are enqueued (a graph keeps the pointer it
+ * was captured with).
+ * Replaces: SeedlessMetal's stopFlag buffer, checked on entry by every
+ * gqmm2 / router kernel (SeedlessMetal.swift:60, 69-70, 2185, 2730). */
+int momij_set_stop_flag(const int32_t* device_flag);
+
+/* Bound of the device-side waits (polls of an mbarrier or of the grid
+ * barrier) before a kernel gives up with MOMIJ_ERR_TIMEOUT: 0 restores the
+ * default (about a second), -1 makes every wait give up at once (for testing
+ * the error path).  Process-wide; applies to calls enqueued afterwards.  No
+ * counterpart in the reference (Metal command buffers have no such bound). */
+int momij_set_spin_limit(int polls);
+
 /* Waits for `stream`, then folds any device-detected error recorded in
  * `workspace` (may be NULL) into the returned status. */
 int momij_moe_synchronize(momij_stream_t stream, const void* workspace);

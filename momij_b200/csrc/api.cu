@@ -8,12 +8,15 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
+#include <cudaTypedefs.h>
 #include <mutex>
+#include <unordered_map>
 #include <vector>
 
 #include "kernels.cuh"
 #include "gemv_core.cuh"
-#include "layer.cuh"
+#include "decode.cuh"
 #include "prefill.cuh"
 
 using namespace momij;
@@ -174,55 +177,115 @@ Workspace carve(void* ws, int M, int Ktop, int H, int I) {
     return w;
 }
 
-// ---- fused MoE layer (layer.cu) -------------------------------------------
+// ---- fused decode layer (decode.cu) ------------------------------------------
 constexpr int kNotApplicable = -1;
 
-LayerArgs layer_args(const float* logits, const int32_t* inds_in, const float* scores_in,
-                     int32_t* inds_out, float* scores_out, const void* x, const uint32_t* w_ug,
-                     const void* s_ug, const void* b_ug, const uint32_t* w_dn, const void* s_dn,
-                     const void* b_dn, void* y, void* resid_h, int M, int H, int I, int E, int K,
-                     float clamp) {
-    LayerArgs a{};
-    a.logits = logits;
-    a.inds_in = inds_in;
-    a.scores_in = scores_in;
-    a.inds_out = inds_out;
-    a.scores_out = scores_out;
-    a.x = static_cast<const uint16_t*>(x);
-    a.w_ug = w_ug;
-    a.s_ug = static_cast<const uint16_t*>(s_ug);
-    a.b_ug = static_cast<const uint16_t*>(b_ug);
-    a.w_dn = w_dn;
-    a.s_dn = static_cast<const uint16_t*>(s_dn);
-    a.b_dn = static_cast<const uint16_t*>(b_dn);
-    a.y = resid_h ? nullptr : static_cast<uint16_t*>(y);
-    a.h = static_cast<uint16_t*>(resid_h);
-    a.M = M;
-    a.H = H;
-    a.I = I;
-    a.E = E;
-    a.K = K;
-    a.clamp = clamp;
-    return a;
+// Process-wide stop flag (the reference's stopFlag buffer, SeedlessMetal.swift:
+// 60, 69-70) and the bound of the kernels' device-side waits.
+std::atomic<const int32_t*> g_stop_flag{nullptr};
+std::atomic<int> g_spin_limit{0};
+constexpr int kDefaultSpinLimit = 1 << 22;
+int spin_limit() {
+    const int v = g_spin_limit.load();
+    if (v != 0) return v > 0 ? v : 0;
+    static const int env = [] {
+        const char* e = std::getenv("MOMIJ_SPIN_LIMIT");
+        const long n = e ? std::strtol(e, nullptr, 10) : 0;
+        return n > 0 && n < (1L << 30) ? (int)n : kDefaultSpinLimit;
+    }();
+    return env;
 }
 
-using LayerFn = void (*)(const LayerArgs);
+// cuTensorMapEncodeTiled from the driver (the runtime is linked statically).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// Tensor maps of packed-code tensors seen as bytes [rows, row_bytes], 128-byte
+// swizzle, box 128 B x box_rows, cached per (device, address, shape, box).
+struct MapKey {
+    int dev;
+    const void* ptr;
+    long long rows;
+    int row_bytes, box_rows;
+    bool operator==(const MapKey& o) const {
+        return dev == o.dev && ptr == o.ptr && rows == o.rows && row_bytes == o.row_bytes && box_rows == o.box_rows;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey& k) const {
+        return std::hash<const void*>()(k.ptr) ^ (std::hash<long long>()(k.rows) * 31) ^
+               ((size_t)k.row_bytes << 20) ^ ((size_t)k.box_rows << 8) ^ (size_t)k.dev;
+    }
+};
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+bool code_map(const void* ptr, long long rows, int row_bytes, int box_rows, CUtensorMap* out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    const MapKey key{dev, ptr, rows, row_bytes, box_rows};
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+        *out = it->second;
+        return true;
+    }
+    auto enc = tensor_map_encoder();
+    if (!enc) return false;
+    cuuint64_t gdim[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    cuuint64_t gstride[1] = {(cuuint64_t)row_bytes};
+    cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUtensorMap m;
+    if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), gdim, gstride, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    if (g_maps.size() >= 8192) g_maps.clear();
+    g_maps.emplace(key, m);
+    *out = m;
+    return true;
+}
+
+struct LayerCall {
+    const float* logits;
+    const int32_t* inds_in;
+    const float* scores_in;
+    int32_t* inds_out;
+    float* scores_out;
+    const void* x;
+    const uint32_t *w_ug, *w_dn;
+    const void *s_ug, *b_ug, *s_dn, *b_dn;
+    void* y;
+    void* resid_h;
+    int M, H, I, E, K;
+    float clamp;
+};
+
+using DecodeFn = void (*)(const DecodeArgs);
 
 template <int DT, int GS>
-LayerFn pick_layer_tm(int tmax) {
-    switch (tmax) {
-        case 1: return moe_layer_kernel<DT, GS, 1, layer_stages(1)>;
-        case 2: return moe_layer_kernel<DT, GS, 2, layer_stages(2)>;
-        case 4: return moe_layer_kernel<DT, GS, 4, layer_stages(4)>;
-        default: return moe_layer_kernel<DT, GS, 8, layer_stages(8)>;
+DecodeFn pick_decode_t(int T) {
+    switch (T) {
+        case 1: return moe_decode_kernel<DT, GS, 1>;
+        case 2: return moe_decode_kernel<DT, GS, 2>;
+        case 4: return moe_decode_kernel<DT, GS, 4>;
+        default: return moe_decode_kernel<DT, GS, 8>;
     }
 }
-LayerFn pick_layer(int dtype, int gs, int tmax) {
+DecodeFn pick_decode(int dtype, int gs, int T) {
     if (dtype == MOMIJ_DTYPE_BF16)
-        return gs == 64 ? pick_layer_tm<MOMIJ_DTYPE_BF16, 64>(tmax)
-                        : pick_layer_tm<MOMIJ_DTYPE_BF16, 128>(tmax);
-    return gs == 64 ? pick_layer_tm<MOMIJ_DTYPE_F16, 64>(tmax)
-                    : pick_layer_tm<MOMIJ_DTYPE_F16, 128>(tmax);
+        return gs == 64 ? pick_decode_t<MOMIJ_DTYPE_BF16, 64>(T) : pick_decode_t<MOMIJ_DTYPE_BF16, 128>(T);
+    return gs == 64 ? pick_decode_t<MOMIJ_DTYPE_F16, 64>(T) : pick_decode_t<MOMIJ_DTYPE_F16, 128>(T);
 }
 
 // Phase tracing of fused-layer launches (momij_layer_trace).
@@ -233,7 +296,7 @@ size_t g_trace_slots = 0, g_trace_next = 0;
 long long* next_trace_slot(int G) {
     std::lock_guard<std::mutex> lk(g_trace_mu);
     if (!g_trace_buf || g_trace_slots == 0) return nullptr;
-    long long* p = g_trace_buf + (g_trace_next % g_trace_slots) * (size_t)G * kTracePoints;
+    long long* p = g_trace_buf + (g_trace_next % g_trace_slots) * (size_t)G * kTracePointsDec;
     ++g_trace_next;
     return p;
 }
@@ -243,131 +306,115 @@ bool fused_enabled() {
     return !(v && v[0] == '0');
 }
 
+// Static shared memory of the decode kernel (DecShared and the kernel's own).
+constexpr int kDecStaticReserve = 8192;
+
 // Launches the whole layer as one cooperative kernel when the batch is a
 // decode/verify batch that fits; kNotApplicable lets the caller fall back to
-// the multi-kernel path (same arithmetic, same bits).
-int run_fused_layer(LayerArgs a, int dtype, int gs, const Workspace& ws, cudaStream_t st) {
-    const int P = a.M * a.K;
-    if (!fused_enabled() || a.M > 8 || P > kLayerMaxPairs || a.E > 1024 || a.K > 32)
+// the multi-kernel path.
+int run_fused_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, cudaStream_t st) {
+    const int P = c.M * c.K;
+    if (!fused_enabled() || c.M > 8 || P > kDecMaxPairs || c.E > 256 || c.K > 32 || c.H < 512 || c.I < 512 ||
+        c.I % 64 || c.H % 128)
         return kNotApplicable;
-    const int tmax = pick_tmax(a.M);
-    const int stages = layer_stages(tmax);
-    const int rt = item_tiles(tmax);
     const int G = current_device_sm_count();
-    if (G <= 0) return kNotApplicable;
-    a.nK_up = a.H / kChunk;
-    a.nK_dn = a.I / kChunk;
-    // rank top-k when its comparisons stay within ~256 per thread
-    a.route_parts = 0;
-    if ((long long)a.M * a.E * a.E <= (long long)kLayerThreads * 256) {
-        int parts = 1;
-        while (parts < 32 && (long long)a.M * a.E * parts * 2 <= kLayerThreads && a.E % (parts * 2) == 0)
-            parts *= 2;
-        a.route_parts = parts;
-    }
-    const long long rows_up = ((long long)P * a.I + G - 1) / G;
-    const long long rows_dn = ((long long)P * a.H + G - 1) / G;
-    const int mu_up = (int)std::min<long long>(P, rows_up / a.I + 2);
-    const int mu_dn = (int)std::min<long long>(P, rows_dn / a.H + 2);
-    const int mt_up = (int)(rows_up / 8 + mu_up + 1);
-    const int mt_dn = (int)(rows_dn / 16 + mu_dn + 1);
-    if (rows_dn / 64 + 2 * mu_dn > kLayerMaxLastBlocks) return kNotApplicable;
-    const int max_units = std::max(mu_up, mu_dn), max_tiles = std::max(mt_up, mt_dn);
-    const int vec_dn = std::min(P, mu_dn * tmax);
-    a.max_tiles = max_tiles;
-    a.max_units = max_units;
-    a.max_vec = vec_dn;
-    const size_t ndg = std::max((size_t)a.M * (a.H / 64), (size_t)vec_dn * (a.I / 64));
-    const size_t limit = (size_t)max_dyn_smem();
-    {
-        size_t off = 0;
-        a.off_logits = (int)off; off += a.logits ? 4 * (size_t)a.M * a.E : 0;
-        a.off_inds = (int)off; off += 4 * (size_t)P;
-        a.off_scores = (int)off; off += 4 * (size_t)P;
-        a.off_sorted = (int)off; off += 4 * (size_t)P;
-        off = align_up(off, 16);
-        a.off_pflag = (int)off; off += 16 * (size_t)P;  // per sorted pair: (expert, before, count)
-        a.off_units = (int)off; off += 16 * (size_t)P;
-        a.off_tiles_up = (int)off; off += 16 * (size_t)max_tiles;
-        a.off_lunits_up = (int)off; off += 16 * (size_t)max_units;
-        a.off_seg_up = (int)off; off += 16 * (size_t)max_units;
-        a.off_tiles_dn = (int)off; off += 16 * (size_t)max_tiles;
-        a.off_lunits_dn = (int)off; off += 16 * (size_t)max_units;
-        a.off_seg_dn = (int)off; off += 16 * (size_t)max_units;
-        a.off_upair_up = (int)off; off += 4 * (size_t)max_units * tmax;
-        a.off_uslot_up = (int)off; off += 4 * (size_t)max_units * tmax;
-        a.off_upair_dn = (int)off; off += 4 * (size_t)max_units * tmax;
-        a.off_uslot_dn = (int)off; off += 4 * (size_t)max_units * tmax;
-        a.off_xvecs = (int)off; off += 4 * (size_t)a.M;
-        a.off_vecs_dn = (int)off; off += 4 * (size_t)vec_dn;
-        off = align_up(off, 16);
-        a.off_fs = (int)off; off += 8 * ndg;
-        off = align_up(off, 16);
-        a.off_dig = (int)off; off += (size_t)kDgStride * ndg;
-        off = align_up(off, 16);
-        // the red and scale/bias buffers take what the ring leaves, up to a
-        // whole phase per batch; the phases share them
-        const size_t ring = (size_t)kConsumerWarps * stages * slot_bytes(tmax);
-        if (off + ring + 256 > limit) return kNotApplicable;
-        const size_t avail = limit - off - ring - 256;
-        const size_t rpt_up = 4 * (size_t)((a.nK_up + 1) / 2) * tmax * red_row(tmax),
-                     rpt_dn = 4 * (size_t)((a.nK_dn + 1) / 2) * tmax * red_row(tmax);  // red_floats_per_tile
-        const size_t spt_up = sb_bytes_per_tile(a.H, gs, tmax == 1), spt_dn = sb_bytes_per_tile(a.I, gs, tmax == 1);
-        size_t bu = (size_t)(mt_up + rt - 1) / rt * rt, bd = (size_t)(mt_dn + rt - 1) / rt * rt;
-        auto need = [&]() {
-            return std::max(bu * rpt_up, bd * rpt_dn) + std::max(bu * spt_up, bd * spt_dn) + 16;
-        };
-        while (need() > avail && (bu > (size_t)rt || bd > (size_t)rt)) {
-            if (bu * (rpt_up + spt_up) >= bd * (rpt_dn + spt_dn) && bu > (size_t)rt) bu = std::max((size_t)rt, (bu / 2 + rt - 1) / rt * rt);
-            else bd = std::max((size_t)rt, (bd / 2 + rt - 1) / rt * rt);
-        }
-        if (need() > avail) return kNotApplicable;
-        a.batch_up = (int)bu;
-        a.batch_dn = (int)bd;
-        a.off_red = (int)off; off += std::max(bu * rpt_up, bd * rpt_dn);
-        off = align_up(off, 16);
-        a.off_sb = (int)off; off += std::max(bu * spt_up, bd * spt_dn);
-        off = align_up(off, 128);
-        a.off_stage = (int)off; off += ring;
-        LayerFn fn = pick_layer(dtype, gs, tmax);
-        if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)off) !=
-            cudaSuccess)
-            return MOMIJ_ERR_CUDA;
-        int per_sm = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kLayerThreads, off) !=
-                cudaSuccess ||
-            per_sm < 1)
+    if (G <= 0 || P > G) return kNotApplicable;  // a CTA's slice then spans at most two units
+    const int T = pick_tmax(c.M);
+    const int N = dec_mma_n(T);
+    const int nG_up = c.H / 64, nG_dn = c.I / 64;
+    // tiles per CTA: rows of the slice / tile height, + 1 for a unit boundary
+    const long long rows_up = ((long long)P * c.I / 8 + G - 1) / G * 8;
+    const long long rows_dn = ((long long)P * c.H / 8 + G - 1) / G * 8;
+    if (rows_up / 64 + 2 > kDecMaxTiles || rows_dn / 128 + 2 > kDecMaxTiles ||
+        rows_dn / 64 + 4 > kDecMaxLastBlocks)
+        return kNotApplicable;
+
+    DecodeArgs a{};
+    for (int i = 0; i < kDecBoxes; ++i) {
+        const int br = 64 >> i;
+        if (!code_map(c.w_ug, (long long)c.E * 2 * c.I, c.H / 4, br, &a.map_ug[i]) ||
+            !code_map(c.w_dn, (long long)c.E * c.H, c.I / 4, br, &a.map_dn[i]))
             return kNotApplicable;
-        a.trace = next_trace_slot(G);
-        a.ctrl = ws.plan;
-        a.ctrl_u = reinterpret_cast<unsigned*>(ws.plan);
-        a.block_ctr = ws.block_ctr;
-        a.act = ws.act;
-        a.down = ws.down;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(G);
-        cfg.blockDim = dim3(kLayerThreads);
-        cfg.dynamicSmemBytes = off;
-        cfg.stream = st;
-        cudaLaunchAttribute attr[2];
-        attr[0].id = cudaLaunchAttributeCooperative;
-        attr[0].val.cooperative = 1;
-        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[1].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        static bool pdl_with_coop = true;  // dropped if the driver refuses the pair
-        cfg.numAttrs = (pdl_enabled() && pdl_with_coop) ? 2 : 1;
-        const int slot = prof_begin(MOMIJ_KERNEL_LAYER, st);
-        cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a);
-        if (e != cudaSuccess && cfg.numAttrs == 2) {
-            cudaGetLastError();
-            pdl_with_coop = false;
-            cfg.numAttrs = 1;
-            e = cudaLaunchKernelEx(&cfg, fn, a);
-        }
-        prof_end(slot, st);
-        return cuda_status(e);
     }
+    a.logits = c.logits;
+    a.inds_in = c.inds_in;
+    a.scores_in = c.scores_in;
+    a.inds_out = c.inds_out;
+    a.scores_out = c.scores_out;
+    a.x = static_cast<const uint16_t*>(c.x);
+    a.s_ug = static_cast<const uint16_t*>(c.s_ug);
+    a.b_ug = static_cast<const uint16_t*>(c.b_ug);
+    a.s_dn = static_cast<const uint16_t*>(c.s_dn);
+    a.b_dn = static_cast<const uint16_t*>(c.b_dn);
+    a.act = ws.act;
+    a.down = ws.down;
+    a.y = c.resid_h ? nullptr : static_cast<uint16_t*>(c.y);
+    a.h = static_cast<uint16_t*>(c.resid_h);
+    a.ctrl = ws.plan;
+    a.block_ctr = ws.block_ctr;
+    a.stop = g_stop_flag.load();
+    a.trace = next_trace_slot(G);
+    a.M = c.M;
+    a.H = c.H;
+    a.I = c.I;
+    a.E = c.E;
+    a.K = c.K;
+    a.gs = gs;
+    a.spin_limit = spin_limit();
+    a.clamp = c.clamp;
+
+    // shared memory: ring | B | per-group factors | scale/bias words | logits
+    const size_t b_bytes = (size_t)std::max(nG_up, 2 * nG_dn) * dec_b_group_bytes(N);
+    const size_t fs_bytes = align_up(8 * (size_t)std::max(c.M * nG_up, 2 * T * nG_dn), 16);
+    const size_t sb_bytes = 16384;  // [4 chunks][4 warpgroups][2][128] words; >= 4 T 128 floats
+    const size_t lg_bytes = align_up(4 * (size_t)(c.logits ? c.M * c.E : 0), 16);
+    const size_t fixed = align_up(b_bytes, 1024) + fs_bytes + sb_bytes + lg_bytes + 1024;
+    int optin = 0, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    const long long room = (long long)optin - kDecStaticReserve - (long long)fixed;
+    int stages = (int)std::min<long long>(kDecMaxStages, room / kDecStageBytes) & ~1;
+    if (stages < 2) return kNotApplicable;
+    size_t off = 0;
+    a.off_ring = (int)off; off += (size_t)stages * kDecStageBytes;
+    a.off_b = (int)off; off += align_up(b_bytes, 1024);
+    a.off_fs = (int)off; off += fs_bytes;
+    a.off_sb = (int)off; off += sb_bytes;
+    a.off_logits = (int)off; off += lg_bytes;
+    const size_t smem = off + 1024;  // + alignment of the base to 1024 B
+    a.stages = stages;
+    a.b_bytes = (int)b_bytes;
+
+    DecodeFn fn = pick_decode(dtype, gs, T);
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return MOMIJ_ERR_CUDA;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kDecThreadsAll, smem) != cudaSuccess ||
+        per_sm < 1)
+        return kNotApplicable;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(kDecThreadsAll);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    static bool pdl_with_coop = true;  // dropped if the driver refuses the pair
+    cfg.numAttrs = (pdl_enabled() && pdl_with_coop) ? 2 : 1;
+    const int slot = prof_begin(MOMIJ_KERNEL_LAYER, st);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a);
+    if (e != cudaSuccess && cfg.numAttrs == 2) {
+        cudaGetLastError();
+        pdl_with_coop = false;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, fn, a);
+    }
+    prof_end(slot, st);
+    return cuda_status(e);
 }
 
 // ---- gather-GEMV dispatch --------------------------------------------------
@@ -732,7 +779,7 @@ int momij_layer_trace(void* device_buffer, size_t bytes) {
         return device_buffer ? MOMIJ_ERR_INVALID_ARGUMENT : MOMIJ_OK;
     }
     g_trace_buf = static_cast<long long*>(device_buffer);
-    g_trace_slots = bytes / ((size_t)G * kTracePoints * sizeof(long long));
+    g_trace_slots = bytes / ((size_t)G * kTracePointsDec * sizeof(long long));
     g_trace_next = 0;
     return g_trace_slots ? MOMIJ_OK : MOMIJ_ERR_WORKSPACE;
 }
@@ -744,6 +791,17 @@ int momij_profile_reset(void) {
 }
 
 int momij_device_sm_count(void) { return current_device_sm_count(); }
+
+int momij_set_stop_flag(const int32_t* device_flag) {
+    g_stop_flag.store(device_flag);
+    return MOMIJ_OK;
+}
+
+int momij_set_spin_limit(int polls) {
+    if (polls < -1) return MOMIJ_ERR_INVALID_ARGUMENT;
+    g_spin_limit.store(polls);
+    return MOMIJ_OK;
+}
 
 int momij_moe_synchronize(momij_stream_t stream, const void* workspace) {
     if (cudaStreamSynchronize(static_cast<cudaStream_t>(stream)) != cudaSuccess) return MOMIJ_ERR_CUDA;
@@ -926,9 +984,9 @@ int momij_moe_expert_ffn(const void* x, const uint32_t* w_ug, const void* s_ug, 
     if (grouped_enabled(M, Ktop, E))
         return run_grouped(x, w_ug, s_ug, b_ug, w_dn, s_dn, b_dn, inds, scores, y, resid_h, M, H, I, E,
                            Ktop, gs, clamp, dtype, ws, st);
-    LayerArgs la = layer_args(nullptr, inds, scores, nullptr, nullptr, x, w_ug, s_ug, b_ug, w_dn,
-                              s_dn, b_dn, y, resid_h, M, H, I, E, Ktop, clamp);
-    const int frc = run_fused_layer(la, dtype, gs, ws, st);
+    const LayerCall lc{nullptr, inds, scores, nullptr, nullptr, x, w_ug, w_dn, s_ug, b_ug, s_dn, b_dn,
+                       y, resid_h, M, H, I, E, Ktop, clamp};
+    const int frc = run_fused_layer(lc, dtype, gs, ws, st);
     if (frc != kNotApplicable) return frc;
     const int tmax = tmax_for(M, Ktop, 0);
     int rc = launch_plan(inds, M * Ktop, E, tmax, ws.plan, st);
@@ -964,9 +1022,9 @@ int momij_moe_forward(const float* logits, const void* x, const uint32_t* w_ug, 
         return run_grouped(x, w_ug, s_ug, b_ug, w_dn, s_dn, b_dn, ind_out, sc_out, y, resid_h, M, H, I,
                            E, Ktop, gs, clamp, dtype, ws, st);
     }
-    LayerArgs la = layer_args(logits, nullptr, nullptr, ind_out, sc_out, x, w_ug, s_ug, b_ug, w_dn,
-                              s_dn, b_dn, y, resid_h, M, H, I, E, Ktop, clamp);
-    const int frc = run_fused_layer(la, dtype, gs, ws, st);
+    const LayerCall lc{logits, nullptr, nullptr, ind_out, sc_out, x, w_ug, w_dn, s_ug, b_ug, s_dn, b_dn,
+                       y, resid_h, M, H, I, E, Ktop, clamp};
+    const int frc = run_fused_layer(lc, dtype, gs, ws, st);
     if (frc != kNotApplicable) return frc;
     const int tmax = tmax_for(M, Ktop, 0);
     const int slot = prof_begin(MOMIJ_KERNEL_PLAN, st);

@@ -1,93 +1,128 @@
 // route_core.cuh -- router top-k of one token by one warp, shared by the
-// router kernels (route.cu) and the fused layer kernel (layer.cu).
+// router kernels (route.cu) and the fused decode-layer kernel (decode.cu).
 //
-// Semantics follow maple_route_top8 (momij SeedlessMetal.swift:2720-2791):
-// K rounds of argmax on the logits where a strictly larger value replaces
-// the running best (so the lower expert index keeps a tie); scores are the
-// selected softmax gates renormalised by their sum.  The softmax denominator
-// cancels in that renormalisation, so the scores are computed directly as
-// exp(l_k - l_max) / sum_selected exp(l_j - l_max) (fp32).
+// Selection follows maple_route_top8 (momij SeedlessMetal.swift:2720-2791)
+// exactly: K rounds, each a reduction tree over a threadgroup of W = 256
+// positions (expert e at position e; positions >= E hold -inf; a selected
+// expert becomes -inf) in which, at stage s = W/2, ..., 1, position t < s takes
+// the candidate of position t + s only if its value is strictly greater
+// (:2764-2775).  Among equal values the tree therefore keeps the expert whose
+// index bits, read from the lowest bit up, are smallest (the minimum of the
+// bit-reversed index) -- not the lowest index: with ties at experts 2 and 4
+// the stage s = 4 gives position 0 expert 4 (if expert 0 is smaller) and the
+// stages s = 2 and 1 keep it.  Signed zeros compare equal and a NaN never
+// replaces nor is replaced, as with the reference's '>'.  The tree is
+// emulated stage by stage here (W/32 positions per lane, then the lane
+// stages by shuffles); for E > 256 (beyond the reference's kernel) the width
+// is the next power of two.
 //
-// The selection is split from the scores so that a caller on a critical
-// path (the fused layer kernel) can start streaming the selected experts'
-// weights before the exponentials are evaluated.
+// Scores follow the reference's staging: softmax gates e_i / Z over all
+// experts (e_i = exp(l_i - max)), the selected gates divided by their sum
+// taken in k order (:2755-2790).
 #pragma once
 
 #include "common.cuh"
 
 namespace momij {
 
-// Order-preserving 64-bit key of (logit, expert): larger logit first, and on
-// equal logits the lower expert index first.
-__device__ __forceinline__ unsigned long long route_key(float v, int e) {
-    uint32_t u = __float_as_uint(v);
-    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)e);
-}
-__device__ __forceinline__ int route_key_expert(unsigned long long k) {
-    return (int)(0xffffffffu - (uint32_t)(k & 0xffffffffull));
+__host__ __device__ inline int route_tree_width(int E) {
+    int W = 256;
+    while (W < E) W <<= 1;
+    return W;
 }
 
-// Top-K indices of one token (one warp; E <= 1024, K <= 32), in descending
-// logit order: inds[k] for k < K (written by lanes 0..K-1).  Each lane keeps
-// its best remaining key; a round is one warp max-reduction, and only the
-// winning lane rescans its (<= 32) logits.
-__device__ __forceinline__ void route_topk_warp(const float* __restrict__ lg, int E, int K,
+// Top-K indices of one token (one warp; E <= 32 * J, K <= 32), in the
+// reference's selection order: inds[k] for k < K (written by lane 0).
+// Positions >= E and experts already selected take no further part (the
+// reference marks them -inf, which differs only when fewer than K finite
+// logits remain).
+template <int J>
+__device__ __forceinline__ void route_topk_tree(const float* __restrict__ lg, int E, int K,
                                                 int* __restrict__ inds) {
     const int lane = threadIdx.x & 31;
-    const int nv = (E + 31) >> 5;
-    uint32_t taken = 0;
-    auto lane_best = [&]() -> unsigned long long {
-        unsigned long long best = 0ull;
-        for (int i = 0; i < nv; ++i) {
-            const int e = lane + 32 * i;
-            if (e < E && !((taken >> i) & 1u)) {
-                const unsigned long long k = route_key(lg[e], e);
-                best = k > best ? k : best;
+    const int W = route_tree_width(E), Jw = W >> 5;  // positions per lane (<= J)
+    float val[J];
+    uint32_t present = 0;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int e = lane + 32 * j;
+        const bool in = j < Jw && e < E;
+        val[j] = in ? lg[e] : -INFINITY;
+        present |= (in ? 1u : 0u) << j;
+    }
+    for (int k = 0; k < K; ++k) {
+        float v[J];
+        int jx[J];
+        bool pr[J];
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            v[j] = val[j];
+            jx[j] = j;
+            pr[j] = (present >> j) & 1u;
+        }
+        // stages s >= 32: positions lane + 32 j and lane + 32 (j + sj), in the lane
+#pragma unroll
+        for (int sj = J / 2; sj >= 1; sj >>= 1) {
+            if (sj < Jw) {
+#pragma unroll
+                for (int j = 0; j < sj; ++j) {
+                    if (pr[j + sj] && (!pr[j] || v[j + sj] > v[j])) {
+                        v[j] = v[j + sj];
+                        jx[j] = jx[j + sj];
+                        pr[j] = true;
+                    }
+                }
             }
         }
-        return best;
-    };
-    unsigned long long mine = lane_best();
-    int my_ind = 0;
-    for (int k = 0; k < K; ++k) {
-        unsigned long long best = mine;
+        // stages s = 16 .. 1: position lane takes lane + s
+        float bv = v[0];
+        int bi = lane + 32 * jx[0];
+        bool bp = pr[0];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
-            best = other > best ? other : best;
+        for (int s = 16; s >= 1; s >>= 1) {
+            const float ov = __shfl_down_sync(0xffffffffu, bv, s);
+            const int oi = __shfl_down_sync(0xffffffffu, bi, s);
+            const bool op = __shfl_down_sync(0xffffffffu, bp ? 1 : 0, s) != 0;
+            if (lane < s && op && (!bp || ov > bv)) {
+                bv = ov;
+                bi = oi;
+                bp = true;
+            }
         }
-        const int e = route_key_expert(best);
-        if (lane == k) my_ind = e;
-        if ((e & 31) == lane) {
-            taken |= 1u << (e >> 5);
-            mine = lane_best();
-        }
+        bi = __shfl_sync(0xffffffffu, bi, 0);
+        if (lane == 0) inds[k] = bi;
+        if ((bi & 31) == lane) present &= ~(1u << (bi >> 5));
     }
-    if (lane < K) inds[lane] = my_ind;
 }
 
-// Renormalised scores of the K selected experts (inds[0] holds the largest
-// logit).  One warp; lanes 0..K-1 write scores[k].
-__device__ __forceinline__ void route_scores_warp(const float* __restrict__ lg, int K,
+// Renormalised scores of the K selected experts.  One warp; lanes 0..K-1
+// write scores[k].
+__device__ __forceinline__ void route_scores_warp(const float* __restrict__ lg, int E, int K,
                                                   const int* __restrict__ inds,
                                                   float* __restrict__ scores) {
     const int lane = threadIdx.x & 31;
-    const float mx = lg[inds[0]];
-    const float ex = (lane < K) ? expf(lg[inds[lane]] - mx) : 0.f;
-    // sum in k order (lane 0 first), as the reference's sequential renorm
-    float s = 0.f;
-    for (int k = 0; k < K; ++k) s += __shfl_sync(0xffffffffu, ex, k);
-    if (lane < K) scores[lane] = ex / s;
+    float mx = -INFINITY;
+    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float z = 0.f;
+    for (int e = lane; e < E; e += 32) z += expf(lg[e] - mx);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) z += __shfl_xor_sync(0xffffffffu, z, o);
+    const float gate = (lane < K) ? expf(lg[inds[lane]] - mx) / z : 0.f;
+    float s = 0.f;  // sum in k order (lane 0 first), as the reference's sequential renorm
+    for (int k = 0; k < K; ++k) s += __shfl_sync(0xffffffffu, gate, k);
+    if (lane < K) scores[lane] = gate / s;
 }
 
 // Both steps for one token.
 __device__ __forceinline__ void route_token_warp(const float* __restrict__ lg, int E, int K,
                                                  int32_t* __restrict__ inds,
                                                  float* __restrict__ scores) {
-    route_topk_warp(lg, E, K, inds);
+    if (E <= 256) route_topk_tree<8>(lg, E, K, inds);
+    else route_topk_tree<32>(lg, E, K, inds);
     __syncwarp();
-    route_scores_warp(lg, K, inds, scores);
+    route_scores_warp(lg, E, K, inds, scores);
 }
 
 }  // namespace momij

@@ -1,0 +1,92 @@
+// tc.cuh -- sm_100a primitives: tensor memory (tcgen05.alloc/ld/st), the
+// tcgen05 MMA issued by one thread, TMA tensor loads into this CTA's shared
+// memory (no multicast), and bounded mbarrier waits.
+#pragma once
+
+#include "common.cuh"
+
+namespace momij {
+
+// ---- tensor memory -----------------------------------------------------------
+// A warp may touch only its lane quarter: lanes 32 (warp % 4) .. + 31.
+__device__ __forceinline__ uint32_t tmem_lane_base(int warp) { return (uint32_t)((warp & 3) * 32) << 16; }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols));
+}
+__device__ __forceinline__ void tc_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 16 consecutive 32-bit columns of this thread's lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---- tcgen05 MMA -------------------------------------------------------------
+// Shared-memory matrix descriptor, K-major, no swizzle: 8-row x 16-byte core
+// matrices; lbo = byte distance of core matrices adjacent along K, sbo = along
+// M/N (8-row groups).
+__device__ __forceinline__ uint64_t sdesc_noswz(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46);
+}
+// Instruction descriptor, kind::i8: s32 accumulator, A unsigned 8-bit, B signed
+// 8-bit, both K-major, M = 128, N = n (a multiple of 16).
+__host__ __device__ constexpr uint32_t idesc_u8s8(int n) {
+    return (2u << 4) | (0u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+// D[tmem d] (+)= A[tmem a] (128 x 32 u8, row m in lane m, 4 k per column) * B[smem desc]^T.
+__device__ __forceinline__ void mma_i8_ta(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+        "r"(a), "l"(bdesc), "r"(idesc), "r"(accum));
+}
+// Arrives (once) on `bar` when every tcgen05 MMA this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// ---- TMA (tensor maps over this GPU's memory, loads into this CTA only) -------
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(dst),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ---- bounded waits -----------------------------------------------------------
+// Spins on `bar` until the phase with `parity` completed, at most `limit`
+// polls; gives up early once *abort is set by another role.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int limit,
+                                                  const volatile int* abort) {
+    for (int it = 0; it < limit; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 255) == 255 && *abort) return false;
+    }
+    return false;
+}
+
+}  // namespace momij

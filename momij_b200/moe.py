@@ -68,6 +68,8 @@ def _load() -> ctypes.CDLL:
     L.momij_moe_ep_combine.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, vp, vp]
     L.momij_synth_fill.argtypes = [vp, ctypes.c_int64, i, f, f, ctypes.c_uint64,
                                    ctypes.c_uint64, ctypes.c_int64, i, vp]
+    L.momij_set_stop_flag.argtypes = [vp]
+    L.momij_set_spin_limit.argtypes = [i]
     L.momij_profile_enable.argtypes = [i]
     L.momij_layer_trace.argtypes = [vp, sz]
     L.momij_profile_read.argtypes = [i, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(i)]
@@ -129,6 +131,20 @@ def new_workspace(M: int, Ktop: int, H: int, I: int, device=None) -> torch.Tenso
 
 def synchronize(stream=None, workspace: torch.Tensor | None = None) -> None:
     _check(lib.momij_moe_synchronize(_stream(stream), _ptr(workspace)), "synchronize")
+
+
+def set_stop_flag(flag: torch.Tensor | None) -> None:
+    """Process-wide stop flag (a device int32 tensor, or None): non-zero makes
+    every later call skip its work and report STOPPED (the reference's
+    stopFlag buffer)."""
+    if flag is not None and (flag.dtype != torch.int32 or not flag.is_cuda):
+        raise TypeError("the stop flag is a CUDA int32 tensor")
+    _check(lib.momij_set_stop_flag(_ptr(flag)), "set_stop_flag")
+
+
+def set_spin_limit(polls: int) -> None:
+    """Bound of the device-side waits (0: default, -1: give up at once)."""
+    _check(lib.momij_set_spin_limit(int(polls)), "set_spin_limit")
 
 
 # ---- router -----------------------------------------------------------------

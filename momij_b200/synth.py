@@ -130,6 +130,23 @@ def expert_weights(E: int, H: int, I: int, gs: int = 64, layer: int = 0, seed: i
     }
 
 
+def expert_weights_one(e: int, H: int, I: int, gs: int = 64, layer: int = 0, seed: int = 0,
+                       dtype: int = DT_BF16) -> dict:
+    """Expert e's slice of expert_weights(E, ...) for any E > e (the same
+    elements of the same streams), without generating the other experts."""
+    out = {}
+    for k, kind, shape in (("w_ug", KIND_W_UG, (2 * I, H // 16)), ("w_dn", KIND_W_DN, (H, I // 16))):
+        n = shape[0] * shape[1]
+        out[k] = codes(n, seed, stream_id(layer, kind), e * n).reshape(shape)
+    for k, kind, shape, a, c in (("s_ug", KIND_S_UG, (2 * I, H // gs), SCALE_A, SCALE_C),
+                                 ("b_ug", KIND_B_UG, (2 * I, H // gs), BIAS_A, BIAS_C),
+                                 ("s_dn", KIND_S_DN, (H, I // gs), SCALE_A, SCALE_C),
+                                 ("b_dn", KIND_B_DN, (H, I // gs), BIAS_A, BIAS_C)):
+        n = shape[0] * shape[1]
+        out[k] = affine_uniform(n, a, c, seed, stream_id(layer, kind), dtype, e * n).reshape(shape)
+    return out
+
+
 def activations(M: int, H: int, layer: int = 0, seed: int = 0, dtype: int = DT_BF16) -> np.ndarray:
     return normal_half(M * H, seed, stream_id(layer, KIND_X), dtype).reshape(M, H)
 

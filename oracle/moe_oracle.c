@@ -88,37 +88,66 @@ void oracle_set_num_threads(int n) {
 #endif
 }
 
-/* ---- router (SeedlessMetal.swift:2720-2791, MapleMoE.swift:49-55) -------- */
+/* ---- router (SeedlessMetal.swift:2720-2791, MapleMoE.swift:49-55) --------
+ * Selection restates maple_route_top8's reduction tree (:2764-2775): per
+ * round, positions 0..W-1 (W = 256, the kernel's threadgroup; the next power
+ * of two for E > 256) hold the candidates, and at stage s = W/2 .. 1 position
+ * t < s takes the candidate of t + s only if its value is strictly greater
+ * (float comparison: signed zeros are equal, NaN never replaces and is never
+ * replaced).  Positions >= E and experts already selected take no further
+ * part (the kernel marks them -inf, which only matters when fewer than K
+ * finite logits remain).  Scores: softmax gates exp(l - max) / Z over all
+ * experts, then the selected gates divided by their sum in k order
+ * (:2755-2790). */
+
+static int route_tree_width(int E) {
+    int W = 256;
+    while (W < E) W <<= 1;
+    return W;
+}
 
 int oracle_route(const float* logits, int M, int E, int K, int32_t* inds, float* scores) {
     if (M < 0 || E <= 0 || K <= 0 || K > E) return -1;
+    const int W = route_tree_width(E);
+    float* red = (float*)malloc(sizeof(float) * W);
+    int* ri = (int*)malloc(sizeof(int) * W);
+    unsigned char* live = (unsigned char*)malloc((size_t)W);
+    unsigned char* used = (unsigned char*)malloc((size_t)W);
+    double* sel = (double*)malloc(sizeof(double) * K);
     for (int m = 0; m < M; ++m) {
         const float* lg = logits + (size_t)m * E;
         double mx = -INFINITY;
         for (int e = 0; e < E; ++e) if (lg[e] > mx) mx = lg[e];
         double Z = 0.0;
         for (int e = 0; e < E; ++e) Z += exp((double)lg[e] - mx);
-        unsigned char* used = (unsigned char*)calloc((size_t)E, 1);
-        double sel[1024];
-        double* selp = K <= 1024 ? sel : (double*)malloc(sizeof(double) * K);
+        memset(used, 0, (size_t)W);
         double ss = 0.0;
         for (int k = 0; k < K; ++k) {
-            int bi = -1;
-            double bv = -INFINITY;
-            for (int e = 0; e < E; ++e) {
-                if (used[e]) continue;
-                /* strict '>' scanning upward: the lower index keeps a tie */
-                if (bi < 0 || (double)lg[e] > bv) { bv = lg[e]; bi = e; }
+            for (int t = 0; t < W; ++t) {
+                red[t] = t < E ? lg[t] : -INFINITY;
+                ri[t] = t;
+                live[t] = t < E && !used[t];
             }
+            for (int st = W / 2; st > 0; st >>= 1)
+                for (int t = 0; t < st; ++t)
+                    if (live[t + st] && (!live[t] || red[t + st] > red[t])) {
+                        red[t] = red[t + st];
+                        ri[t] = ri[t + st];
+                        live[t] = 1;
+                    }
+            const int bi = ri[0];
             used[bi] = 1;
             inds[(size_t)m * K + k] = bi;
-            selp[k] = exp((double)lg[bi] - mx) / Z;
-            ss += selp[k];
+            sel[k] = exp((double)lg[bi] - mx) / Z;
+            ss += sel[k];
         }
-        for (int k = 0; k < K; ++k) scores[(size_t)m * K + k] = (float)(selp[k] / ss);
-        if (selp != sel) free(selp);
-        free(used);
+        for (int k = 0; k < K; ++k) scores[(size_t)m * K + k] = (float)(sel[k] / ss);
     }
+    free(red);
+    free(ri);
+    free(live);
+    free(used);
+    free(sel);
     return 0;
 }
 

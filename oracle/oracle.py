@@ -203,13 +203,56 @@ def np_dequant(w: np.ndarray, s: np.ndarray, b: np.ndarray, gs: int, dtype: int 
 
 
 def np_route(logits: np.ndarray, K: int):
-    lg = np.asarray(logits, np.float64)
+    """Independent restatement of the router: the selection order of
+    maple_route_top8's strict-'>' reduction tree (SeedlessMetal.swift:
+    2764-2775) is, among equal values, the smallest bit-reversed index over the
+    tree's width (256, or the next power of two above E); without NaN logits
+    this is a sort by (value descending, bit-reversed index ascending)."""
+    lg32 = np.asarray(logits, np.float32)
+    lg = lg32.astype(np.float64)
     M, E = lg.shape
-    order = np.lexsort((np.broadcast_to(np.arange(E), lg.shape), -lg), axis=1)[:, :K]
+    W = 256
+    while W < E:
+        W *= 2
+    bits = W.bit_length() - 1
+    e = np.arange(E)
+    rev = np.zeros(E, np.int64)
+    for i in range(bits):
+        rev |= ((e >> i) & 1) << (bits - 1 - i)
+    val = np.where(lg == 0.0, 0.0, lg)  # -0 == +0
+    order = np.lexsort((np.broadcast_to(rev, lg.shape), -val), axis=1)[:, :K]
     p = np.exp(lg - lg.max(axis=1, keepdims=True))
     p /= p.sum(axis=1, keepdims=True)
     sel = np.take_along_axis(p, order, axis=1)
     return order.astype(np.int32), (sel / sel.sum(axis=1, keepdims=True)).astype(np.float32)
+
+
+def tree_route_indices(logits_row: np.ndarray, K: int) -> list[int]:
+    """Literal step-by-step replay of maple_route_top8's selection loop
+    (SeedlessMetal.swift:2764-2781) for one token: K rounds of a 256-wide (or
+    wider, for E > 256) reduction in which position t < s takes t + s only if
+    strictly greater; selected experts and positions >= E drop out.  Pure
+    Python: small cases only."""
+    lg = [float(v) for v in np.asarray(logits_row, np.float32)]
+    E = len(lg)
+    W = 256
+    while W < E:
+        W *= 2
+    used = set()
+    out = []
+    for _ in range(K):
+        red = [lg[t] if t < E else float("-inf") for t in range(W)]
+        ri = list(range(W))
+        live = [t < E and t not in used for t in range(W)]
+        s = W // 2
+        while s > 0:
+            for t in range(s):
+                if live[t + s] and (not live[t] or red[t + s] > red[t]):
+                    red[t], ri[t], live[t] = red[t + s], ri[t + s], True
+            s //= 2
+        out.append(ri[0])
+        used.add(ri[0])
+    return out
 
 
 def np_gqmm2(x, w, s, b, inds, M, Ktop, gs, lhs_per_expert=False, dtype=0):

@@ -83,15 +83,47 @@ def test_route_indices_bit_exact(M, E, K):
     np.testing.assert_allclose(scores.cpu().numpy(), s_ref, rtol=2e-6, atol=1e-7)
 
 
-def test_route_ties_prefer_lower_index():
+def tie_heavy_logits(M: int, E: int, seed: int, levels: int = 3) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    vals = np.array([-0.0, 0.0] + [float(v) for v in np.linspace(-1.0, 1.0, levels)], np.float32)
+    return vals[rng.integers(0, len(vals), size=(M, E))].astype(np.float32)
+
+
+def test_route_ties_follow_the_reference_tree():
     lg = np.zeros((3, 64), np.float32)
     lg[0, [7, 3, 40, 41]] = 2.0
+    lg[1, 3], lg[1, 5] = -0.0, 0.0
+    lg[1, [0, 1, 2, 4]] = -1.0
+    lg[1, 6:] = -1.0
     lg[2, :] = -1.0
     inds, scores = moe.route(torch.from_numpy(lg).to(DEV), 6)
     i_ref, s_ref = O.route(lg, 6)
-    assert (inds.cpu().numpy() == i_ref).all()
-    assert inds.cpu().numpy()[0, :4].tolist() == [3, 7, 40, 41]
+    got = inds.cpu().numpy()
+    assert (got == i_ref).all()
+    for m in range(3):
+        assert got[m].tolist() == O.tree_route_indices(lg[m], 6)
+    assert got[0, :4].tolist() == [40, 41, 3, 7]  # bit-reversed order of the tied experts
+    assert got[1, :2].tolist() == [5, 3]          # -0.0 and +0.0 tie
     np.testing.assert_allclose(scores.cpu().numpy(), s_ref, rtol=2e-6)
+
+
+@pytest.mark.parametrize("M,E,K", [(4, 16, 8), (8, 128, 8), (3, 256, 16), (2, 300, 8)])
+def test_route_tie_heavy_logits_bit_exact(M, E, K):
+    lg = tie_heavy_logits(M, E, seed=7 * E + K)
+    inds, _ = moe.route(torch.from_numpy(lg).to(DEV), K)
+    i_ref, _ = O.route(lg, K)
+    assert (inds.cpu().numpy() == i_ref).all()
+
+
+def test_route_nan_logits_follow_the_tree():
+    lg = S.logits_normal(3, 128, seed=11)
+    lg[0, 0] = np.nan   # position 0 keeps a NaN: selected first
+    lg[1, 5] = np.nan   # a NaN at position 5 is dropped by the stage s = 4
+    lg[2, [7, 70]] = np.nan
+    inds, _ = moe.route(torch.from_numpy(lg).to(DEV), 8)
+    got = inds.cpu().numpy()
+    for m in range(3):
+        assert got[m].tolist() == O.tree_route_indices(lg[m], 8)
 
 
 def test_permute_matches_oracle():
@@ -235,22 +267,26 @@ def test_fused_expert_matches_oracle(M, H, I, E, K, gs, dt):
     (3, 768, 1536, 24, 6, 128, 1, 0.7),
     (5, 4096, 256, 32, 8, 64, 0, None),
 ])
-def test_fused_layer_matches_multikernel_path(M, H, I, E, K, gs, dt, rho, monkeypatch):
+def test_fused_layer_and_multikernel_path_match_oracle(M, H, I, E, K, gs, dt, rho, monkeypatch):
     """The one-kernel decode layer (route + up + grid barrier + down +
-    last-arriver combine) and the multi-kernel path (route/plan, up, down,
-    combine kernels) run the same arithmetic: same bits, several calls in a
-    row on one workspace (the completion counters reset themselves)."""
+    last-arriver combine on the tcgen05 tensor cores) and the multi-kernel
+    path (route/plan, up, down, combine kernels on the GEMV engine) both match
+    the oracle, call after call on one workspace (the grid-barrier and
+    completion counters return to zero); repeated calls of the fused layer
+    give the same bits."""
     w = S.expert_weights(E, H, I, gs, seed=13, dtype=dt)
     dw = dev_weights(w, dt)
     ws = moe.new_workspace(M, K, H, I)
     outs = {}
     for path in ("1", "0"):
         monkeypatch.setenv("MOMIJ_FUSED", path)
-        for call in range(3):
-            x = S.activations(M, H, layer=call, seed=13, dtype=dt)
-            lg = (S.logits_ar1(M, E, rho, call, 13) if rho else S.logits_normal(M, E, call, 13))
+        for call in range(4):
+            lay = call % 2  # calls 2 and 3 repeat the inputs of calls 0 and 1
+            x = S.activations(M, H, layer=lay, seed=13, dtype=dt)
+            lg = (S.logits_ar1(M, E, rho, lay, 13) if rho else S.logits_normal(M, E, lay, 13))
             y = torch.empty(M, H, dtype=TD[dt], device=DEV)
-            h = dev16(S.normal_half(M * H, 13, 99, dt).reshape(M, H), dt)
+            h0 = S.normal_half(M * H, 13, 99, dt).reshape(M, H)
+            h = dev16(h0, dt)
             inds = torch.empty(M, K, dtype=torch.int32, device=DEV)
             scores = torch.empty(M, K, dtype=torch.float32, device=DEV)
             moe.forward(torch.from_numpy(lg).to(DEV), dev16(x, dt), dw, y, H=H, I=I, Ktop=K, gs=gs,
@@ -259,17 +295,15 @@ def test_fused_layer_matches_multikernel_path(M, H, I, E, K, gs, dt, rho, monkey
                         gs=gs, M=M, resid_h=h, workspace=ws)
             moe.synchronize(workspace=ws)
             outs[(path, call)] = (host16(y), host16(h), inds.cpu().numpy(), scores.cpu().numpy())
-    for call in range(3):
-        f, m = outs[("1", call)], outs[("0", call)]
-        for a, b in zip(f, m):
+            i_ref, s_ref = O.route(lg, K)
+            y_ref, st = O.expert_ffn(x, w, i_ref, s_ref, M, H, I, K, gs, 7.0, dt)
+            h_ref, _ = O.expert_ffn(x, w, i_ref, s_ref, M, H, I, K, gs, 7.0, dt, resid_h=h0)
+            assert (outs[(path, call)][2] == i_ref).all()
+            assert_ffn_parity(outs[(path, call)][0], y_ref, st["down"], s_ref, dt, f"path {path} call {call}")
+            assert_ffn_parity(outs[(path, call)][1], h_ref, st["down"], s_ref, dt, f"path {path} call {call} resid")
+    for call in (2, 3):
+        for a, b in zip(outs[("1", call)], outs[("1", call - 2)]):
             assert (a == b).all(), call
-    # and against the oracle
-    x = S.activations(M, H, layer=0, seed=13, dtype=dt)
-    lg = (S.logits_ar1(M, E, rho, 0, 13) if rho else S.logits_normal(M, E, 0, 13))
-    i_ref, s_ref = O.route(lg, K)
-    y_ref, st = O.expert_ffn(x, w, i_ref, s_ref, M, H, I, K, gs, 7.0, dt)
-    assert (outs[("1", 0)][2] == i_ref).all()
-    assert_ffn_parity(outs[("1", 0)][0], y_ref, st["down"], s_ref, dt, "fused layer")
 
 
 def test_fused_expert_mrow_matches_sequential():

@@ -39,7 +39,15 @@ def test_c_oracle_matches_numpy_restatement(M, H, I, E, K, gs, dt):
     assert (y == y2).all()
 
 
-def test_route_matches_numpy_and_breaks_ties_low():
+def tie_heavy_logits(M: int, E: int, seed: int, levels: int = 3) -> np.ndarray:
+    """Logits drawn from a few values (with signed zeros) so that most
+    selections are decided by the router's tie rule."""
+    rng = np.random.default_rng(seed)
+    vals = np.array([-0.0, 0.0] + [float(v) for v in np.linspace(-1.0, 1.0, levels)], np.float32)
+    return vals[rng.integers(0, len(vals), size=(M, E))].astype(np.float32)
+
+
+def test_route_matches_numpy_and_the_reference_tree():
     lg = S.logits_normal(16, 128, seed=3)
     i1, s1 = O.route(lg, 8)
     i2, s2 = O.np_route(lg, 8)
@@ -49,14 +57,30 @@ def test_route_matches_numpy_and_breaks_ties_low():
     # descending logit order
     sel = np.take_along_axis(lg, i1, axis=1)
     assert (np.diff(sel, axis=1) <= 0).all()
-    # exact ties: the lower index wins (strict '>' in maple_route_top8)
-    t = np.zeros((2, 16), np.float32)
+    # exact ties go where maple_route_top8's strict-'>' tree puts them: the
+    # smallest bit-reversed index, not the lowest index
+    t = np.zeros((3, 16), np.float32)
     t[0, [3, 5, 9]] = 1.0
     t[1, :] = -2.0
+    t[2, :] = -1.0
+    t[2, 3], t[2, 5] = -0.0, 0.0  # signed zeros tie
     it, st = O.route(t, 4)
-    assert it[0].tolist() == [3, 5, 9, 0]
-    assert it[1].tolist() == [0, 1, 2, 3]
+    assert it[0].tolist() == [9, 5, 3, 0]
+    assert it[1].tolist() == [0, 8, 4, 12]
+    assert it[2].tolist() == [5, 3, 0, 8]
     np.testing.assert_allclose(st[1], 0.25, rtol=1e-7)
+    for m in range(3):
+        assert it[m].tolist() == O.tree_route_indices(t[m], 4)
+
+
+@pytest.mark.parametrize("E,K", [(16, 8), (64, 8), (128, 8), (256, 16), (300, 8)])
+def test_route_follows_the_literal_tree_on_ties(E, K):
+    lg = tie_heavy_logits(6, E, seed=E + K)
+    i1, _ = O.route(lg, K)
+    i2, _ = O.np_route(lg, K)
+    assert (i1 == i2).all()
+    for m in range(lg.shape[0]):
+        assert i1[m].tolist() == O.tree_route_indices(lg[m], K)
 
 
 def test_permute_is_a_stable_counting_sort():
