@@ -209,30 +209,37 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// Tensor maps of packed-code tensors seen as bytes [rows, row_bytes], 128-byte
-// swizzle, box 128 B x box_rows, cached per (device, address, shape, box).
+// Tensor maps of weight tensors seen as bytes [rows, row_bytes]: packed codes
+// with 128-byte swizzle and boxes 128 B wide, scales and biases without
+// swizzle and boxes 16 B wide; box_rows rows.  halves > 0: a 3D view [E*2
+// halves, half_rows, row_bytes] whose box takes box_rows rows of two
+// consecutive halves (the up and the gate rows of one expert).  Cached per
+// (device, address, shape, box).
 struct MapKey {
     int dev;
     const void* ptr;
     long long rows;
-    int row_bytes, box_rows;
+    int row_bytes, box_rows, box_bytes, half_rows;
     bool operator==(const MapKey& o) const {
-        return dev == o.dev && ptr == o.ptr && rows == o.rows && row_bytes == o.row_bytes && box_rows == o.box_rows;
+        return dev == o.dev && ptr == o.ptr && rows == o.rows && row_bytes == o.row_bytes && box_rows == o.box_rows &&
+               box_bytes == o.box_bytes && half_rows == o.half_rows;
     }
 };
 struct MapKeyHash {
     size_t operator()(const MapKey& k) const {
         return std::hash<const void*>()(k.ptr) ^ (std::hash<long long>()(k.rows) * 31) ^
-               ((size_t)k.row_bytes << 20) ^ ((size_t)k.box_rows << 8) ^ (size_t)k.dev;
+               ((size_t)k.row_bytes << 20) ^ ((size_t)k.box_rows << 8) ^ ((size_t)k.box_bytes << 40) ^
+               ((size_t)k.half_rows << 44) ^ (size_t)k.dev;
     }
 };
 std::mutex g_map_mu;
 std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 
-bool code_map(const void* ptr, long long rows, int row_bytes, int box_rows, CUtensorMap* out) {
+bool weight_map(const void* ptr, long long rows, int row_bytes, int box_bytes, int box_rows, int half_rows,
+                CUtensorMap* out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return false;
-    const MapKey key{dev, ptr, rows, row_bytes, box_rows};
+    const MapKey key{dev, ptr, rows, row_bytes, box_rows, box_bytes, half_rows};
     std::lock_guard<std::mutex> lk(g_map_mu);
     auto it = g_maps.find(key);
     if (it != g_maps.end()) {
@@ -241,18 +248,38 @@ bool code_map(const void* ptr, long long rows, int row_bytes, int box_rows, CUte
     }
     auto enc = tensor_map_encoder();
     if (!enc) return false;
-    cuuint64_t gdim[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
-    cuuint64_t gstride[1] = {(cuuint64_t)row_bytes};
-    cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
-    cuuint32_t estr[2] = {1, 1};
     CUtensorMap m;
-    if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), gdim, gstride, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-        return false;
+    const CUtensorMapSwizzle swz = box_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE;
+    CUresult r;
+    if (half_rows > 0) {
+        cuuint64_t gdim[3] = {(cuuint64_t)row_bytes, (cuuint64_t)half_rows, (cuuint64_t)(rows / half_rows)};
+        cuuint64_t gstride[2] = {(cuuint64_t)row_bytes, (cuuint64_t)row_bytes * (cuuint64_t)half_rows};
+        cuuint32_t box[3] = {(cuuint32_t)box_bytes, (cuuint32_t)box_rows, 2};
+        cuuint32_t estr[3] = {1, 1, 1};
+        r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(ptr), gdim, gstride, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        cuuint64_t gdim[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+        cuuint64_t gstride[1] = {(cuuint64_t)row_bytes};
+        cuuint32_t box[2] = {(cuuint32_t)box_bytes, (cuuint32_t)box_rows};
+        cuuint32_t estr[2] = {1, 1};
+        r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), gdim, gstride, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (r != CUDA_SUCCESS) return false;
     if (g_maps.size() >= 8192) g_maps.clear();
     g_maps.emplace(key, m);
     *out = m;
+    return true;
+}
+
+// The five maps of one weight tensor (decode.cuh: kDecMaps): 2D boxes of 64,
+// 16, 8 and 128 rows, and (up||gate only) the 3D box of 64 rows x 2 halves.
+bool weight_maps(const void* ptr, long long rows, int row_bytes, int box_bytes, int half_rows, CUtensorMap* maps) {
+    const int heights[4] = {64, 16, 8, 128};
+    for (int i = 0; i < 4; ++i)
+        if (!weight_map(ptr, rows, row_bytes, box_bytes, heights[i], 0, &maps[i])) return false;
+    if (half_rows > 0) return weight_map(ptr, rows, row_bytes, box_bytes, 64, half_rows, &maps[4]);
     return true;
 }
 
@@ -314,8 +341,7 @@ constexpr int kDecStaticReserve = 8192;
 // the multi-kernel path.
 int run_fused_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, cudaStream_t st) {
     const int P = c.M * c.K;
-    if (!fused_enabled() || c.M > 8 || P > kDecMaxPairs || c.E > 256 || c.K > 32 || c.H < 512 || c.I < 512 ||
-        c.I % 64 || c.H % 128)
+    if (!fused_enabled() || c.M > 8 || P > kDecMaxPairs || c.E > 256 || c.K > 32 || c.H % 512 || c.I % 512)
         return kNotApplicable;
     const int G = current_device_sm_count();
     if (G <= 0 || P > G) return kNotApplicable;  // a CTA's slice then spans at most two units
@@ -329,23 +355,23 @@ int run_fused_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, 
         rows_dn / 64 + 4 > kDecMaxLastBlocks)
         return kNotApplicable;
 
+    // TMA row strides are multiples of 16 bytes: the scale rows (Kd / gs halves) too
+    if ((c.H / gs * 2) % 16 || (c.I / gs * 2) % 16) return kNotApplicable;
     DecodeArgs a{};
-    for (int i = 0; i < kDecBoxes; ++i) {
-        const int br = 64 >> i;
-        if (!code_map(c.w_ug, (long long)c.E * 2 * c.I, c.H / 4, br, &a.map_ug[i]) ||
-            !code_map(c.w_dn, (long long)c.E * c.H, c.I / 4, br, &a.map_dn[i]))
-            return kNotApplicable;
-    }
+    const long long wrows_ug = (long long)c.E * 2 * c.I, wrows_dn = (long long)c.E * c.H;
+    if (!weight_maps(c.w_ug, wrows_ug, c.H / 4, 128, c.I, a.map_ug) ||
+        !weight_maps(c.s_ug, wrows_ug, c.H / gs * 2, 16, c.I, a.map_sug) ||
+        !weight_maps(c.b_ug, wrows_ug, c.H / gs * 2, 16, c.I, a.map_bug) ||
+        !weight_maps(c.w_dn, wrows_dn, c.I / 4, 128, 0, a.map_dn) ||
+        !weight_maps(c.s_dn, wrows_dn, c.I / gs * 2, 16, 0, a.map_sdn) ||
+        !weight_maps(c.b_dn, wrows_dn, c.I / gs * 2, 16, 0, a.map_bdn))
+        return kNotApplicable;
     a.logits = c.logits;
     a.inds_in = c.inds_in;
     a.scores_in = c.scores_in;
     a.inds_out = c.inds_out;
     a.scores_out = c.scores_out;
     a.x = static_cast<const uint16_t*>(c.x);
-    a.s_ug = static_cast<const uint16_t*>(c.s_ug);
-    a.b_ug = static_cast<const uint16_t*>(c.b_ug);
-    a.s_dn = static_cast<const uint16_t*>(c.s_dn);
-    a.b_dn = static_cast<const uint16_t*>(c.b_dn);
     a.act = ws.act;
     a.down = ws.down;
     a.y = c.resid_h ? nullptr : static_cast<uint16_t*>(c.y);
@@ -363,24 +389,30 @@ int run_fused_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, 
     a.spin_limit = spin_limit();
     a.clamp = c.clamp;
 
-    // shared memory: ring | B | per-group factors | scale/bias words | logits
+    // shared memory: ring of stages (codes + scales + biases) | B | per-group
+    // factors | scale/bias stash | tile-end partials; the logits and router
+    // keys live in the ring (the producers start only after the routing)
     const size_t b_bytes = (size_t)std::max(nG_up, 2 * nG_dn) * dec_b_group_bytes(N);
     const size_t fs_bytes = align_up(8 * (size_t)std::max(c.M * nG_up, 2 * T * nG_dn), 16);
-    const size_t sb_bytes = 16384;  // [4 chunks][4 warpgroups][2][128] words; >= 4 T 128 floats
+    const size_t stash_bytes = (size_t)2 * kDecStash * 128 * 16;
+    const size_t red_bytes = (size_t)2 * T * 128 * 4;
     const size_t lg_bytes = align_up(4 * (size_t)(c.logits ? c.M * c.E : 0), 16);
-    const size_t fixed = align_up(b_bytes, 1024) + fs_bytes + sb_bytes + lg_bytes + 1024;
+    const size_t key_bytes = align_up(8 * (size_t)(c.logits ? c.M * c.E : 0), 16);
+    const size_t fixed = align_up(b_bytes, 1024) + fs_bytes + stash_bytes + red_bytes + 1024;
     int optin = 0, dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     const long long room = (long long)optin - kDecStaticReserve - (long long)fixed;
     int stages = (int)std::min<long long>(kDecMaxStages, room / kDecStageBytes) & ~1;
-    if (stages < 2) return kNotApplicable;
+    if (stages < 2 || (size_t)stages * kDecStageBytes < lg_bytes + key_bytes) return kNotApplicable;
     size_t off = 0;
     a.off_ring = (int)off; off += (size_t)stages * kDecStageBytes;
     a.off_b = (int)off; off += align_up(b_bytes, 1024);
     a.off_fs = (int)off; off += fs_bytes;
-    a.off_sb = (int)off; off += sb_bytes;
-    a.off_logits = (int)off; off += lg_bytes;
+    a.off_stash = (int)off; off += stash_bytes;
+    a.off_red = (int)off; off += red_bytes;
+    a.off_logits = a.off_ring;
+    a.off_keys = a.off_ring + (int)lg_bytes;
     const size_t smem = off + 1024;  // + alignment of the base to 1024 B
     a.stages = stages;
     a.b_bytes = (int)b_bytes;

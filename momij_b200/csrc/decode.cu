@@ -41,12 +41,34 @@ constexpr int kBarDec = 1;         // named barrier of the 512 dequantising thre
 constexpr int kDrainLimit = 1 << 24;  // polls while draining copies / MMAs on an error path
 constexpr int kGridSpinNs = 64;
 
-__device__ __forceinline__ void dstamp(const DecodeArgs& a, int i) {
-    if (a.trace && threadIdx.x == 0) {
+__device__ __forceinline__ void dstamp_thread(const DecodeArgs& a, int i) {
+    if (a.trace) {
         unsigned long long t;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
         a.trace[(size_t)blockIdx.x * kTracePointsDec + i] = (long long)t;
     }
+}
+__device__ __forceinline__ void dstamp(const DecodeArgs& a, int i) {
+    if (threadIdx.x == 0) dstamp_thread(a, i);
+}
+
+__device__ __forceinline__ long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return (long long)t;
+}
+// Accumulated wait time of one role, written to trace slot `i` (tracing only).
+__device__ __forceinline__ void dwait_put(const DecodeArgs& a, int i, long long ns) {
+    if (a.trace) a.trace[(size_t)blockIdx.x * kTracePointsDec + i] = ns;
+}
+
+__device__ __forceinline__ int ld_acquire_shared(const volatile int* p) {
+    int v;
+    asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_u32((const void*)p)) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_add_shared(int* p, int v) {
+    asm volatile("red.release.cta.shared::cta.add.s32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
@@ -90,26 +112,6 @@ __device__ __forceinline__ uint32_t route_value_key(float v) {
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 __device__ __forceinline__ uint32_t rev_index(int e, int rb) { return __brev((uint32_t)e) >> (32 - rb); }
-
-// Ranks all M*E candidates block-wide (tokens without NaN logits): candidate
-// (m, e) lands at position r = #{e' : e' wins over e} when r < K.
-__device__ void route_ranks(const float* s_logits, const int* s_nan, int M, int E, int K, int rb,
-                            int nthreads, int* s_inds) {
-    const int ncand = M * E;
-    for (int c = threadIdx.x; c < ncand; c += nthreads) {
-        const int m = c / E, e = c - m * E;
-        if (s_nan[m]) continue;
-        const float* lg = s_logits + m * E;
-        const uint32_t ok = route_value_key(lg[e]);
-        const uint32_t re = rev_index(e, rb);
-        int r = 0;
-        for (int j = 0; j < E; ++j) {
-            const uint32_t oj = route_value_key(lg[j]);
-            r += (oj > ok) | ((oj == ok) & (rev_index(j, rb) < re));
-        }
-        if (r < K) s_inds[m * K + r] = e;
-    }
-}
 
 // ---- work plan ------------------------------------------------------------
 // Sort the P <= 64 pairs by (expert, pair) and cut each expert's run into
@@ -187,9 +189,10 @@ __device__ int make_tiles(int r0, int r1, int rows_per_unit, int tile_rows, int4
 __device__ __forceinline__ int b_off(int N, int h, int n, int k) {
     return h * 32 * N + (n >> 3) * 256 + (k >> 4) * 128 + (n & 7) * 16 + (k & 15);
 }
-// Slot of group g in its accumulator pack of GP groups: the packs of a
-// warpgroup hold its consecutive groups (two per 8-group chunk).
-__device__ __forceinline__ int pack_slot(int g, int GP) { return (2 * (g >> 3) + (g & 1)) & (GP - 1); }
+// Slot of group g in its accumulator pack of GP (<= 4) groups: a warpgroup
+// takes four consecutive groups of every 8-group chunk, so its packs hold
+// consecutive groups.
+__device__ __forceinline__ int pack_slot(int g, int GP) { return g & (GP - 1); }
 
 // Balanced base-256 digits of |y| < 2^29: y = 2^24 d0 + 2^16 d1 + 2^8 d2 + d3.
 __device__ __forceinline__ void split4(int y, int (&d)[4]) {
@@ -203,40 +206,38 @@ __device__ __forceinline__ void split4(int y, int (&d)[4]) {
 
 // Writes the digits of vectors src[v] (row length Kd, `nvec` of them, vector
 // v in column set v) into B (groups [0, Kd/64)) and their per-group factors
-// fs[v * nG + g] = (2^(E-27), sum of the group).  Eight lanes per (vector,
-// group); `nthreads` threads from thread 0 take part.  Loads bypass L1 (the
-// vectors may have been written by other CTAs).
+// fs[v * nG + g] = (2^(E-27), sum of the group).  Sixteen lanes per (vector,
+// group): lane (w, p) takes the elements 16w + 4b + p, b = 0..3 -- the four
+// K-bytes of one column word of every digit row -- so each digit is one
+// 32-bit store.  `nthreads` threads from thread t0 take part.  Loads bypass
+// L1 (the vectors may have been written by other CTAs).
 template <int DT>
-__device__ void digitize_b(const uint16_t* const* src, int nvec, int Kd, int N, int T, unsigned char* B,
-                           float2* fs, int nthreads) {
+__device__ void digitize_b(const uint16_t* const* src, int nvec, int Kd, int N, int T, int GP, unsigned char* B,
+                           float2* fs, int nthreads, int t0 = 0) {
     const int nG = Kd >> 6;
-    const int GP = N / (4 * T);
-    const int total = nvec * nG * 8;
+    const int total = nvec * nG * 16;
     const int lane = threadIdx.x & 31;
     const int gbytes = dec_b_group_bytes(N);
-    for (int base = (threadIdx.x & ~31); base < total; base += nthreads) {
+    for (int base = ((threadIdx.x - t0) & ~31); base < total; base += nthreads) {
         const int idx = base + lane;
         const bool valid = idx < total;
-        const int vg = idx >> 3, sub = idx & 7;
+        const int vg = idx >> 4, sub = idx & 15;
+        const int w = sub >> 2, p = sub & 3;
         const int v = valid ? vg / nG : 0, g = valid ? vg - v * nG : 0;
-        float xv[8];
+        float xv[4];
         float mx = 0.f, sum = 0.f;
         if (valid) {
-            const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(src[v] + (size_t)g * 64 + sub * 8));
-            const uint32_t r[4] = {raw.x, raw.y, raw.z, raw.w};
+            const uint16_t* xg = src[v] + (size_t)g * 64 + 16 * w + p;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                xv[2 * i] = Half<DT>::to_f(static_cast<uint16_t>(r[i] & 0xffffu));
-                xv[2 * i + 1] = Half<DT>::to_f(static_cast<uint16_t>(r[i] >> 16));
-            }
+            for (int b = 0; b < 4; ++b) xv[b] = Half<DT>::to_f(__ldcg(xg + 4 * b));
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                mx = fmaxf(mx, fabsf(xv[i]));
-                sum += xv[i];
+            for (int b = 0; b < 4; ++b) {
+                mx = fmaxf(mx, fabsf(xv[b]));
+                sum += xv[b];
             }
         }
 #pragma unroll
-        for (int o = 1; o < 8; o <<= 1) {
+        for (int o = 1; o < 16; o <<= 1) {
             mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
             sum += __shfl_xor_sync(0xffffffffu, sum, o);
         }
@@ -244,18 +245,23 @@ __device__ void digitize_b(const uint16_t* const* src, int nvec, int Kd, int N, 
         int E = (mx > 0.f) ? ilogbf(mx) : 0;
         E = max(E, -100);
         const float scale = ldexpf(1.f, 21 - E);
-        unsigned char* Bg = B + (size_t)g * gbytes;
+        uint32_t word[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int X = __float2int_rn(xv[b] * scale);
+            int dg[4];
+            split4(X << (2 * (3 - p)), dg);
+#pragma unroll
+            for (int dd = 0; dd < 4; ++dd) word[dd] |= (uint32_t)(dg[dd] & 0xff) << (8 * b);
+        }
+        // element 16w + 4b + p: MMA half h = p >> 1, column word c = 4 (p & 1) + w, byte b
+        const int h = p >> 1, c = 4 * (p & 1) + w;
         const int nb = pack_slot(g, GP) * 4 * T + v * 4;
+        unsigned char* Bh = B + (size_t)g * gbytes + h * 32 * N + (c >> 2) * 128 + (c & 3) * 4;
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            const int e = sub * 8 + t;
-            const int i = e >> 4, b = (e >> 2) & 3, p = e & 3;
-            const int h = p >> 1, c = 4 * (p & 1) + i, k = 4 * c + b;
-            const int X = __float2int_rn(xv[t] * scale);
-            int d[4];
-            split4(X << (2 * (3 - p)), d);
-#pragma unroll
-            for (int dd = 0; dd < 4; ++dd) Bg[b_off(N, h, nb + dd, k)] = static_cast<unsigned char>(d[dd] & 0xff);
+        for (int dd = 0; dd < 4; ++dd) {
+            const int n = nb + dd;
+            *reinterpret_cast<uint32_t*>(Bh + (n >> 3) * 256 + (n & 7) * 16) = word[dd];
         }
         if (sub == 0) fs[v * nG + g] = make_float2(ldexpf(1.f, E - 27), sum);
     }
@@ -265,6 +271,7 @@ __device__ void digitize_b(const uint16_t* const* src, int nvec, int Kd, int N, 
 // Warp-uniform bounded wait: every lane polls, and the warp leaves together
 // (all lanes saw the phase) or gives up together.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int limit, const volatile int* abort) {
+    if (__all_sync(0xffffffffu, mbar_test_wait(bar, parity))) return true;  // usually complete already
     for (int it = 0; it < limit; ++it) {
         if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
         if ((it & 255) == 255 && __any_sync(0xffffffffu, *abort != 0)) return false;
@@ -276,6 +283,54 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
     for (int it = 0; it < kDrainLimit; ++it)
         if (mbar_try_wait(bar, parity)) return;
 }
+
+
+// Router of the M tokens by the `nthr` threads from thread `t0` (a named
+// barrier `bar` over them): 64-bit keys (value order, then the reference's
+// tree order on ties: the smaller bit-reversed index) in shared memory, then
+// candidate (m, e) lands at position #{e' : key(e') > key(e)} when that is
+// below K.  Tokens with a NaN logit take the reference's tree step by step
+// (route_topk_tree).  Scores: route_scores_warp.
+__device__ void route_tokens(const float* s_logits, unsigned long long* s_keys, const int* s_nan, int M,
+                             int E, int K, int t0, int nthr, int bar, int* s_inds, float* s_scores,
+                             long long* trace = nullptr) {
+    const int t = threadIdx.x - t0;
+    const int rb = 31 - __clz(route_tree_width(E));
+    for (int c = t; c < M * E; c += nthr) {
+        const int e = c % E;
+        s_keys[c] = ((unsigned long long)route_value_key(s_logits[c]) << 32) |
+                    (unsigned long long)(0xffffffffu - rev_index(e, rb));
+    }
+    bar_sync(bar, nthr);
+    constexpr int kParts = 8;  // threads per candidate
+    for (int base = 0; base < M * E * kParts; base += nthr) {
+        const int it = base + t;
+        const int c = it / kParts, sub = it % kParts;
+        int r = 0;
+        const bool valid = c < M * E;
+        const int m = valid ? c / E : 0;
+        if (valid && !s_nan[m]) {
+            const unsigned long long kc = s_keys[c];
+            const unsigned long long* kr = s_keys + m * E;
+#pragma unroll 8
+            for (int j = sub; j < E; j += kParts) r += kr[j] > kc;
+        }
+#pragma unroll
+        for (int o = 1; o < kParts; o <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+        if (valid && sub == 0 && !s_nan[m] && r < K) s_inds[m * K + r] = c - m * E;
+    }
+    const int w = t >> 5, nw = nthr >> 5;
+    for (int m = w; m < M; m += nw)
+        if (s_nan[m]) route_topk_tree<8>(s_logits + m * E, E, K, s_inds + m * K);
+    bar_sync(bar, nthr);
+    if (trace && t == 0) {
+        unsigned long long tt;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tt));
+        trace[(size_t)blockIdx.x * kTracePointsDec + 25] = (long long)tt;
+    }
+    for (int m = w; m < M; m += nw) route_scores_warp(s_logits + m * E, E, K, s_inds + m * K, s_scores + m * K);
+}
+
 
 struct DecShared {
     int inds[kDecMaxPairs];
@@ -293,11 +348,17 @@ struct DecShared {
     uint32_t tmem;
     alignas(8) uint64_t full[kDecMaxStages];
     alignas(8) uint64_t empty[kDecMaxStages];
-    alignas(8) uint64_t a_full[4][2];
-    alignas(8) uint64_t a_empty[4][2];
-    alignas(8) uint64_t d_full[4][4];
+    // per (warpgroup, A slot): warps of the warpgroup that wrote the slot, over all its
+    // uses (a warp reaches a slot's next use only after its previous MMAs completed,
+    // which needed all four warps' previous writes: the count cannot run ahead)
+    int a_ready[2][kDecAslots];
+    alignas(8) uint64_t a_empty[2][kDecAslots][2];  // [warpgroup][slot][issuing warp]
+    alignas(8) uint64_t d_full[4][4];                // [issuing warp][pack buffer]
     alignas(8) uint64_t d_empty[4][4];
-    alignas(8) uint64_t drain;
+    alignas(8) uint64_t sb_full[2][kDecStash];
+    alignas(8) uint64_t sb_empty[2][kDecStash];
+    alignas(8) uint64_t b_ready[2];
+    alignas(8) uint64_t drain[4];
 };
 
 }  // namespace
@@ -308,11 +369,15 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
     unsigned char* smem =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ DecShared S;
+    // GP groups per accumulator pack; ND pack buffers per issuing warp (64 TMEM columns)
+    constexpr int N = dec_mma_n(T), GP = dec_gp(T), ND = 64 / N;
+    constexpr int kBarEpi = 1, kBarRoute = 2, kBarEnc = 3;
+    constexpr int kWarpEpi0 = kDecDeqWarps, kWarpMma0 = kDecDeqWarps + kDecEpiWarps,
+                  kWarpProd0 = kWarpMma0 + kDecMmaWarps;
+    constexpr int kTidEpi0 = 32 * kWarpEpi0;
     dstamp(a, 0);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int P = a.M * a.K;
-    constexpr int N = dec_mma_n(T), GP = N / (4 * T), ND = 64 / N;
-    const int nthreads = blockDim.x;
     volatile int* abort_flag = &S.abort;
 
     // ---- set-up (independent of the previous kernel) ---------------------------
@@ -320,40 +385,47 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
     if (tid == 0) {
         for (int s = 0; s < a.stages; ++s) {
             mbar_init(&S.full[s], 1);
-            mbar_init(&S.empty[s], kDecWarps);
+            mbar_init(&S.empty[s], kDecDeqWarps);
         }
-        for (int w = 0; w < 4; ++w) {
-            for (int s = 0; s < 2; ++s) {
-                mbar_init(&S.a_full[w][s], 4);
-                mbar_init(&S.a_empty[w][s], 1);
+        for (int d = 0; d < 2; ++d) {
+            for (int s = 0; s < kDecAslots; ++s) S.a_ready[d][s] = 0;
+            for (int s = 0; s < kDecAslots; ++s)
+                for (int h = 0; h < 2; ++h) mbar_init(&S.a_empty[d][s][h], 1);
+            for (int s = 0; s < kDecStash; ++s) {
+                mbar_init(&S.sb_full[d][s], 4);
+                mbar_init(&S.sb_empty[d][s], 4);
             }
+        }
+        for (int i = 0; i < 4; ++i) {
             for (int s = 0; s < 4; ++s) {
-                mbar_init(&S.d_full[w][s], 1);
-                mbar_init(&S.d_empty[w][s], 4);
+                mbar_init(&S.d_full[i][s], 1);
+                mbar_init(&S.d_empty[i][s], 4);
             }
+            mbar_init(&S.drain[i], 1);
         }
-        mbar_init(&S.drain, 1);
+        mbar_init(&S.b_ready[0], 1);
+        mbar_init(&S.b_ready[1], 1);
         mbar_fence_init();
         S.abort = 0;
         S.stopped = 0;
     }
     float* s_logits = reinterpret_cast<float*>(smem + a.off_logits);
+    unsigned long long* s_keys = reinterpret_cast<unsigned long long*>(smem + a.off_keys);
     unsigned char* s_B = smem + a.off_b;
     float2* s_fs = reinterpret_cast<float2*>(smem + a.off_fs);
-    uint32_t* s_sb = reinterpret_cast<uint32_t*>(smem + a.off_sb);  // scale/bias words; tile-end partials
-    float* s_red = reinterpret_cast<float*>(smem + a.off_sb);
+    uint4* s_stash = reinterpret_cast<uint4*>(smem + a.off_stash);  // [2][kDecStash][128] scale|bias words
+    float* s_red = reinterpret_cast<float*>(smem + a.off_red);      // [2][T][128] tile-end partials
     unsigned char* s_ring = smem + a.off_ring;
     tc_before_sync();
     __syncthreads();
     tc_after_sync();
     const uint32_t tmem = S.tmem;
 
-    // ---- routing and plan (after the previous kernel: logits may be its output)
+    // ---- after the previous kernel: x and the logits may be its output ---------
     pdl_wait();
     pdl_launch_dependents();
     dstamp(a, 1);
     if (tid == 0 && a.stop && __ldcg(a.stop) != 0) S.stopped = 1;
-    const int nlog = a.logits ? a.M * a.E : 0;
     if (tid < 8) S.nan_tok[tid] = 0;
     __syncthreads();
     // A set stop flag (the reference's stopFlag, read once per CTA) skips the
@@ -361,112 +433,129 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
     // completion counts, so a flag raised while CTAs start leaves the
     // workspace consistent for the next call.
     const bool stopped = S.stopped != 0;
-    for (int i = tid; i < nlog; i += nthreads) {
-        const float v = __ldcg(a.logits + i);
-        s_logits[i] = v;
-        if (isnan(v)) S.nan_tok[i / a.E] = 1;
-    }
-    if (!a.logits) {
-        for (int i = tid; i < P; i += nthreads) {
-            S.inds[i] = __ldcg(a.inds_in + i);
-            S.scores[i] = __ldcg(a.scores_in + i);
-        }
-    }
-    __syncthreads();
-    if (a.logits) {
-        const int rb = 31 - __clz(route_tree_width(a.E));
-        route_ranks(s_logits, S.nan_tok, a.M, a.E, a.K, rb, nthreads, S.inds);
-        if (warp < a.M && S.nan_tok[warp])  // NaN logits: the reference's tree, stage by stage
-            route_topk_tree<8>(s_logits + warp * a.E, a.E, a.K, S.inds + warp * a.K);
-        __syncthreads();
-    }
-    // plan (warp 0) while warps 1..M compute the routing scores
-    if (warp == 0) {
-        plan_units_warp(S.inds, P, a.E, a.K, T, S.units, S.sorted, S.qinfo, &S.nunits, &S.bad);
-    } else if (a.logits && warp <= a.M) {
-        const int m = warp - 1;
-        route_scores_warp(s_logits + m * a.E, a.E, a.K, S.inds + m * a.K, S.scores + m * a.K);
-    }
-    __syncthreads();
-    const bool ok = S.bad == 0;
-    if (blockIdx.x == 0 && tid == 0) a.ctrl[kCtrlStatus] = ok ? MOMIJ_OK : MOMIJ_ERR_EXPERT_INDEX;
-    if (stopped && ok && tid == 0) a.ctrl[kCtrlStatus] = MOMIJ_ERR_STOPPED;
-    if (!ok) {  // uniform: every CTA sees the same indices
-        if (warp == 0) tmem_dealloc(tmem, kDecTmemCols);
-        return;
-    }
-    dstamp(a, 2);
-    const int U = S.nunits;
-    const int G = gridDim.x, bx = blockIdx.x;
+    const int nG_up = a.H >> 6, nG_dn = a.I >> 6;
+    const int gbytes = dec_b_group_bytes(N);
+    // ---- routing and plan, all threads (the producers need the plan first) ------
     {
-        const long long n8u = (long long)U * a.I / 8, n8d = (long long)U * a.H / 8;
-        const int r0 = (int)(n8u * bx / G) * 8, r1 = (int)(n8u * (bx + 1) / G) * 8;
-        const int d0 = (int)(n8d * bx / G) * 8, d1 = (int)(n8d * (bx + 1) / G) * 8;
+        const int nthr = kDecThreadsAll;
+        const int nlog = a.logits ? a.M * a.E : 0;
+        for (int i = tid; i < nlog; i += nthr) {
+            const float v = __ldcg(a.logits + i);
+            s_logits[i] = v;
+            if (isnan(v)) S.nan_tok[i / a.E] = 1;
+        }
+        if (!a.logits) {
+            for (int i = tid; i < P; i += nthr) {
+                S.inds[i] = __ldcg(a.inds_in + i);
+                S.scores[i] = __ldcg(a.scores_in + i);
+            }
+        }
+        __syncthreads();
+        if (tid == 0) dstamp_thread(a, 22);
+        if (a.logits) route_tokens(s_logits, s_keys, S.nan_tok, a.M, a.E, a.K, 0, nthr, 0, S.inds, S.scores, a.trace);
+        __syncthreads();
+        if (tid == 0) dstamp_thread(a, 23);
+        if (warp == 0) plan_units_warp(S.inds, P, a.E, a.K, T, S.units, S.sorted, S.qinfo, &S.nunits, &S.bad);
+        __syncthreads();
         if (tid == 0) {
+            dstamp_thread(a, 24);
+            const int U = S.nunits, G = gridDim.x, bx = blockIdx.x;
+            const long long n8u = (long long)U * a.I / 8, n8d = (long long)U * a.H / 8;
+            const int r0 = (int)(n8u * bx / G) * 8, r1 = (int)(n8u * (bx + 1) / G) * 8;
+            const int d0 = (int)(n8d * bx / G) * 8, d1 = (int)(n8d * (bx + 1) / G) * 8;
             S.nt_up = make_tiles(r0, r1, a.I, 64, S.tiles_up, kDecMaxTiles);
             S.nt_dn = make_tiles(d0, d1, a.H, 128, S.tiles_dn, kDecMaxTiles);
             S.udn0 = d0 < d1 ? d0 / a.H : 0;
             S.nudn = d0 < d1 ? (d1 - 1) / a.H - d0 / a.H + 1 : 0;
-            if (S.nt_up > kDecMaxTiles || S.nt_dn > kDecMaxTiles || S.nudn > 2) {
+            if (S.bad == 0 && (S.nt_up > kDecMaxTiles || S.nt_dn > kDecMaxTiles || S.nudn > 2)) {
                 atomicExch(a.ctrl + kCtrlError, MOMIJ_ERR_WORKSPACE);  // host-sized; unreachable
                 S.nt_up = S.nt_dn = 0;
                 S.nudn = 0;
             }
+            if (a.trace) a.trace[(size_t)blockIdx.x * kTracePointsDec + 16] = gtime();
         }
-        if (bx == 0) {
-            for (int i = tid; i < P; i += nthreads) {
+        if (blockIdx.x == 0 && S.bad == 0) {
+            for (int i = tid; i < P; i += nthr) {
                 if (a.inds_out) a.inds_out[i] = S.inds[i];
                 if (a.scores_out) a.scores_out[i] = S.scores[i];
             }
         }
     }
     __syncthreads();
-    dstamp(a, 3);
-
-    const int nG_up = a.H >> 6, nG_dn = a.I >> 6;
+    const bool ok = S.bad == 0;
+    if (blockIdx.x == 0 && tid == 0)
+        a.ctrl[kCtrlStatus] = ok ? (stopped ? MOMIJ_ERR_STOPPED : MOMIJ_OK) : MOMIJ_ERR_EXPERT_INDEX;
+    if (!ok) {  // uniform: every CTA sees the same indices
+        if (warp == 0) tmem_dealloc(tmem, kDecTmemCols);
+        return;
+    }
+    dstamp(a, 2);
+    const int U = S.nunits;
     const int nC_up = (nG_up + 7) >> 3, nC_dn = (nG_dn + 7) >> 3;
     // tiles streamed and computed (none when stopped); nt_dn_all also feeds the combine counts
     const int nt_up = stopped ? 0 : S.nt_up, nt_dn = stopped ? 0 : S.nt_dn, nt_dn_all = S.nt_dn;
     const int S_ = a.stages;
+    // groups of warpgroup d in chunk c of a phase with nG groups (0 or 4: nG % 4 == 0)
+    auto wg_groups = [](int nG, int c, int d) { return min(4, max(0, min(8, nG - 8 * c) - 4 * d)); };
 
-    if (warp >= kDecWarps && warp < kDecWarps + kDecProducers) {
-        // ---- TMA producers: item i (phase, tile, chunk) fills stage i % S_; --------
-        // ---- producer i % 2 (S_ is even, so a stage always has the same producer)
+    if (warp >= kWarpProd0) {
+        // ---- TMA producers: item i (phase, tile, chunk) fills stage i % S_ -------------
+        // ---- (codes, then scales, then biases); producer i % 2 (S_ is even) -----------
         if (lane == 0) {
-            const int p = warp - kDecWarps;
+            const int p = warp - kWarpProd0;
             int item = 0;
             int issued_last[kDecMaxStages];
+            long long wait_ns = 0;
             for (int s = 0; s < kDecMaxStages; ++s) issued_last[s] = -1;
             bool okp = true;
             for (int ph = 0; ph < 2 && okp; ++ph) {
                 const int nt = ph ? nt_dn : nt_up, nC = ph ? nC_dn : nC_up;
                 const int4* tiles = ph ? S.tiles_dn : S.tiles_up;
-                const CUtensorMap* maps = ph ? a.map_dn : a.map_ug;
+                const CUtensorMap* mc = ph ? a.map_dn : a.map_ug;
+                const CUtensorMap* ms = ph ? a.map_sdn : a.map_sug;
+                const CUtensorMap* mb = ph ? a.map_bdn : a.map_bug;
                 for (int t = 0; t < nt && okp; ++t) {
                     const int4 tl = tiles[t];
                     const int e = S.units[tl.x].x;
                     for (int c = 0; c < nC; ++c, ++item) {
                         if ((item & 1) != p) continue;
                         const int s = item % S_, use = item / S_;
+                        const long long tw0 = a.trace ? gtime() : 0;
                         if (use > 0 && !mbar_wait_bounded(&S.empty[s], (use - 1) & 1, a.spin_limit, abort_flag)) {
                             okp = false;
                             break;
                         }
-                        const int nparts = ph ? 1 : 2;
-                        mbar_expect_tx(&S.full[s], (uint32_t)(nparts * tl.z * 128));
+                        if (a.trace) wait_ns += gtime() - tw0;
+                        const int rows = ph ? tl.z : 2 * tl.z;
+                        mbar_expect_tx(&S.full[s], (uint32_t)(rows * (128 + 32)));
                         const uint32_t st = smem_u32(s_ring + (size_t)s * kDecStageBytes);
-                        for (int part = 0; part < nparts; ++part) {
-                            // up||gate: up rows at stage rows [0, n), gate rows at [64, 64 + n)
-                            int grow = ph ? e * a.H + tl.y : e * 2 * a.I + part * a.I + tl.y;
-                            int srow = part * 64;
-                            int left = tl.z;
-                            while (left > 0) {
-                                const int bi = left >= 64 ? 0 : left >= 32 ? 1 : left >= 16 ? 2 : 3;
-                                const int br = 64 >> bi;
-                                tma_load_2d(st + srow * 128, &maps[bi], c * 128, grow, &S.full[s]);
-                                grow += br;
-                                srow += br;
-                                left -= br;
+                        const uint32_t ss = st + kDecCodeBytes, sb = ss + kDecSbBytes;
+                        const int xc = c * 128, xs = (GS == 64) ? 16 * c : 16 * (c >> 1);
+                        if (ph == 0 && tl.z == 64) {  // a full up||gate tile: both halves in one box each
+                            tma_load_3d(st, &mc[4], xc, tl.y, 2 * e, &S.full[s]);
+                            tma_load_3d(ss, &ms[4], xs, tl.y, 2 * e, &S.full[s]);
+                            tma_load_3d(sb, &mb[4], xs, tl.y, 2 * e, &S.full[s]);
+                        } else if (ph == 1 && tl.z == 128) {
+                            const int grow = e * a.H + tl.y;
+                            tma_load_2d(st, &mc[3], xc, grow, &S.full[s]);
+                            tma_load_2d(ss, &ms[3], xs, grow, &S.full[s]);
+                            tma_load_2d(sb, &mb[3], xs, grow, &S.full[s]);
+                        } else {
+                            for (int part = 0; part < (ph ? 1 : 2); ++part) {
+                                // up||gate: up rows at stage rows [0, n), gate rows at [64, 64 + n)
+                                int grow = ph ? e * a.H + tl.y : e * 2 * a.I + part * a.I + tl.y;
+                                int srow = part * 64;
+                                int left = tl.z;
+                                while (left > 0) {
+                                    const int bi = left >= 64 ? 0 : left >= 16 ? 1 : 2;
+                                    const int br = bi == 0 ? 64 : bi == 1 ? 16 : 8;
+                                    tma_load_2d(st + srow * 128, &mc[bi], xc, grow, &S.full[s]);
+                                    tma_load_2d(ss + srow * 16, &ms[bi], xs, grow, &S.full[s]);
+                                    tma_load_2d(sb + srow * 16, &mb[bi], xs, grow, &S.full[s]);
+                                    grow += br;
+                                    srow += br;
+                                    left -= br;
+                                }
                             }
                         }
                         issued_last[s] = use;
@@ -477,74 +566,86 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                 *abort_flag = 1;
                 atomicExch(a.ctrl + kCtrlError, MOMIJ_ERR_TIMEOUT);
             }
+            if (p == 0) dwait_put(a, 11, wait_ns);
             // every issued stage has landed before the CTA can exit
             for (int s = 0; s < S_; ++s)
                 if (issued_last[s] >= 0) mbar_drain(&S.full[s], issued_last[s] & 1);
         }
-    } else if (warp == kDecWarps + kDecProducers) {
-        // ---- MMA issuer ------------------------------------------------------
+    } else if (warp >= kWarpMma0) {
+        // ---- MMA issue: warp kWarpMma0 + 2d + hh issues groups 2hh, 2hh + 1 ---------
+        // ---- of warpgroup d's four in every chunk ---------------------------------
         if (lane == 0) {
-            int ua[4] = {0, 0, 0, 0}, ud[4] = {0, 0, 0, 0};
+            const int iw = warp - kWarpMma0, d = iw >> 1, hh = iw & 1;
+            int ua = 0, ud = 0;
+            long long wait_a = 0, wait_d = 0, cy_issue = 0;
             const uint32_t idesc = idesc_u8s8(N);
-            const int gbytes = dec_b_group_bytes(N);
             bool okm = true;
+            const uint32_t tA0 = tmem + d * 256, tD0 = tmem + d * 256 + 128 + hh * 64;
+
             for (int ph = 0; ph < 2 && okm; ++ph) {
                 const int nt = ph ? nt_dn : nt_up, nC = ph ? nC_dn : nC_up, nG = ph ? nG_dn : nG_up;
                 const int4* tiles = ph ? S.tiles_dn : S.tiles_up;
+                if (nt > 0) {  // the phase's digit operand
+                    if (!mbar_wait_bounded(&S.b_ready[ph], 0, a.spin_limit, abort_flag)) {
+                        okm = false;
+                        break;
+                    }
+                }
                 for (int t = 0; t < nt && okm; ++t) {
                     const int4 tl = tiles[t];
-                    const uint32_t bbase =
-                        smem_u32(s_B) + (ph ? (uint32_t)((tl.x - S.udn0) * nG_dn * gbytes) : 0u);
-                    int q[4] = {0, 0, 0, 0};
-                    int nGw[4];
-#pragma unroll
-                    for (int w = 0; w < 4; ++w) {
-                        int n = 0;
-                        for (int c = 0; c < nC; ++c) n += min(2, max(0, min(8, nG - 8 * c) - 2 * w));
-                        nGw[w] = n;
-                    }
+                    const uint32_t bbase = smem_u32(s_B) + (ph ? (uint32_t)((tl.x - S.udn0) * nG_dn * gbytes) : 0u);
                     for (int c = 0; c < nC && okm; ++c) {
-                        const int ngc = min(8, nG - 8 * c);
-#pragma unroll
-                        for (int w = 0; w < 4; ++w) {
-                            const int cnt = min(2, max(0, ngc - 2 * w));
-                            if (cnt == 0 || !okm) continue;
-                            const int slot = ua[w] & 1;
-                            if (!mbar_wait_bounded(&S.a_full[w][slot], (ua[w] >> 1) & 1, a.spin_limit, abort_flag)) {
-                                okm = false;
-                                continue;
-                            }
-                            tc_after_sync();
-                            const uint32_t tA = tmem + w * 128 + slot * 32;
-                            for (int tt = 0; tt < cnt && okm; ++tt) {
-                                const int g = 8 * c + 2 * w + tt;
-                                const int qq = q[w]++;
-                                const int gl = qq & (GP - 1);
-                                const int buf = ud[w] % ND;
-                                if (gl == 0 && ud[w] >= ND) {
-                                    if (!mbar_wait_bounded(&S.d_empty[w][buf], ((ud[w] - ND) / ND) & 1, a.spin_limit,
-                                                           abort_flag)) {
-                                        okm = false;
-                                        continue;
-                                    }
-                                    tc_after_sync();
-                                }
-                                const uint32_t tD = tmem + w * 128 + 64 + buf * N;
-#pragma unroll
-                                for (int h = 0; h < 2; ++h) {
-                                    const uint64_t bd =
-                                        sdesc_noswz(bbase + (uint32_t)(g * gbytes + h * 32 * N), 128, 256);
-                                    mma_i8_ta(tD, tA + tt * 16 + h * 8, bd, idesc, (gl | h) ? 1u : 0u);
-                                }
-                                if (gl == GP - 1 || qq == nGw[w] - 1) {
-                                    mma_commit(&S.d_full[w][buf]);
-                                    ++ud[w];
+                        if (wg_groups(nG, c, d) == 0) continue;
+                        const int slot = ua % kDecAslots;
+                        const long long tw0 = a.trace ? gtime() : 0;
+                        // the four warps of the warpgroup have written the slot (acquire)
+                        {
+                            const int want = 4 * (ua / kDecAslots + 1);
+                            const volatile int* ready = &S.a_ready[d][slot];
+                            int it = 0;
+                            while (ld_acquire_shared(ready) < want) {
+                                if (++it > a.spin_limit || ((it & 255) == 0 && *abort_flag)) {
+                                    okm = false;
+                                    break;
                                 }
                             }
-                            if (!okm) continue;
-                            mma_commit(&S.a_empty[w][slot]);
-                            ++ua[w];
+                            if (!okm) break;
                         }
+                        if (a.trace) wait_a += gtime() - tw0;
+                        tc_after_sync();
+                        const long long cyi = a.trace ? clock64() : 0;
+                        const uint32_t tA = tA0 + slot * 64;
+#pragma unroll
+                        for (int jj = 0; jj < 2; ++jj) {
+                            const int j = 2 * hh + jj;
+                            const int g = 8 * c + 4 * d + j;
+                            const int gl = jj & (GP - 1);
+                            const int buf = ud % ND;
+                            if (gl == 0 && ud >= ND) {
+                                const long long tw1 = a.trace ? gtime() : 0;
+                                if (!mbar_wait_bounded(&S.d_empty[iw][buf], ((ud - ND) / ND) & 1, a.spin_limit,
+                                                       abort_flag)) {
+                                    okm = false;
+                                    break;
+                                }
+                                if (a.trace) wait_d += gtime() - tw1;
+                                tc_after_sync();
+                            }
+                            const uint32_t tD = tD0 + buf * N;
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const uint64_t bd = sdesc_noswz(bbase + (uint32_t)(g * gbytes + h * 32 * N), 128, 256);
+                                mma_i8_ta(tD, tA + j * 16 + h * 8, bd, idesc, (gl | h) ? 1u : 0u);
+                            }
+                            if (gl == GP - 1) {
+                                mma_commit(&S.d_full[iw][buf]);
+                                ++ud;
+                            }
+                        }
+                        if (!okm) break;
+                        mma_commit(&S.a_empty[d][slot][hh]);
+                        if (a.trace) cy_issue += clock64() - cyi;
+                        ++ua;
                     }
                 }
             }
@@ -552,204 +653,247 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                 *abort_flag = 1;
                 atomicExch(a.ctrl + kCtrlError, MOMIJ_ERR_TIMEOUT);
             }
+            if (iw == 0) {
+                dwait_put(a, 12, wait_a);
+                dwait_put(a, 13, wait_d);
+                dwait_put(a, 19, cy_issue);
+            }
             // every MMA issued has completed before the tensor memory is released
-            mma_commit(&S.drain);
-            mbar_drain(&S.drain, 0);
+            mma_commit(&S.drain[iw]);
+            mbar_drain(&S.drain[iw], 0);
+        }
+    } else if (warp < kWarpEpi0) {
+        // ---- dequantising warpgroup d: groups [4d, 4d + 4) of every stage ---------------
+        // ---- (16-byte chunks 4d .. 4d + 3 of a 128-byte stage row); lane L = tile row --
+        const int d = warp >> 2, L = (warp & 3) * 32 + lane;
+        const uint32_t lane_off = tmem_lane_base(warp);
+        const uint32_t tA0 = tmem + d * 256;
+        int item = 0, ua = 0, uc = 0;
+        bool okd = true;
+        long long w_full = 0, w_a = 0;
+        for (int ph = 0; ph < 2; ++ph) {
+            const int nt = ph ? nt_dn : nt_up, nC = ph ? nC_dn : nC_up, nG = ph ? nG_dn : nG_up;
+            for (int t = 0; t < nt; ++t) {
+                for (int c = 0; c < nC; ++c, ++item) {
+                    const int s = item % S_;
+                    const long long tw0 = a.trace ? gtime() : 0;
+                    if (okd) okd = mbar_wait_warp(&S.full[s], (item / S_) & 1, a.spin_limit, abort_flag);
+                    if (a.trace) w_full += gtime() - tw0;
+                    const int cnt = wg_groups(nG, c, d);
+                    uint4 raw[4];
+                    uint2 sbw = make_uint2(0u, 0u);
+                    if (cnt > 0 && okd) {
+                        const unsigned char* stg = s_ring + (size_t)s * kDecStageBytes;
+                        const unsigned char* row = stg + L * 128;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            raw[j] = *reinterpret_cast<const uint4*>(row + (((4 * d + j) ^ (L & 7)) << 4));
+                        // the four groups' scales and biases (gs 128: two scales, one word)
+                        const int so = (GS == 64) ? 8 * d : 8 * (c & 1) + 4 * d;
+                        if (GS == 64) {
+                            sbw.x = *reinterpret_cast<const uint32_t*>(stg + kDecCodeBytes + L * 16 + so);
+                            sbw.y = *reinterpret_cast<const uint32_t*>(stg + kDecCodeBytes + L * 16 + so + 4);
+                        } else {
+                            sbw.x = *reinterpret_cast<const uint32_t*>(stg + kDecCodeBytes + L * 16 + so);
+                        }
+                        uint2 bbw = make_uint2(0u, 0u);
+                        bbw.x = *reinterpret_cast<const uint32_t*>(stg + kDecCodeBytes + kDecSbBytes + L * 16 + so);
+                        if (GS == 64)
+                            bbw.y = *reinterpret_cast<const uint32_t*>(stg + kDecCodeBytes + kDecSbBytes + L * 16 + so + 4);
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&S.empty[s]);  // the stage is in registers now
+                        // scale/bias words for the epilogue warpgroup
+                        const int sl = uc % kDecStash;
+                        if (uc >= kDecStash)
+                            okd = mbar_wait_warp(&S.sb_empty[d][sl], ((uc - kDecStash) / kDecStash) & 1, a.spin_limit,
+                                                 abort_flag);
+                        if (okd) {
+                            s_stash[((size_t)d * kDecStash + sl) * 128 + L] = make_uint4(sbw.x, sbw.y, bbw.x, bbw.y);
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&S.sb_full[d][sl]);
+                        }
+                        ++uc;
+                        // the A operand: four class words per code word, 16 columns per group
+                        const int slot = ua % kDecAslots;
+                        const long long tw1 = a.trace ? gtime() : 0;
+                        for (int h = 0; h < 2; ++h)
+                            if (okd && ua >= kDecAslots)
+                                okd = mbar_wait_warp(&S.a_empty[d][slot][h], ((ua - kDecAslots) / kDecAslots) & 1,
+                                                     a.spin_limit, abort_flag);
+                        if (a.trace) w_a += gtime() - tw1;
+                        if (okd) {
+                            tc_after_sync();
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const uint32_t wv[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+                                uint32_t m[16];
+#pragma unroll
+                                for (int p = 0; p < 4; ++p)
+#pragma unroll
+                                    for (int i = 0; i < 4; ++i) m[4 * p + i] = wv[i] & (0x03030303u << (2 * p));
+                                tmem_st16(tA0 + slot * 64 + j * 16 + lane_off, m);
+                            }
+                            tmem_st_wait();
+                            tc_before_sync();
+                            __syncwarp();
+                            if (lane == 0) red_release_add_shared(&S.a_ready[d][slot], 1);
+                        }
+                        ++ua;
+                    } else {
+                        __syncwarp();
+                        if (lane == 0 && okd) mbar_arrive(&S.empty[s]);
+                    }
+                }
+            }
+        }
+        if (!okd) *abort_flag = 1;
+        if (tid == 0) {
+            dwait_put(a, 14, w_full);
+            dwait_put(a, 15, w_a);
         }
     } else {
-        // ---- 16 dequantising warps: warpgroup wg takes 16-byte chunks 2wg, 2wg+1 --
-        // ---- (groups 8c + 2wg, 8c + 2wg + 1) of every stage; lane L = tile row ----
-        const int wg = warp >> 2, wq = warp & 3, L = wq * 32 + lane;
+        // ---- epilogue warpgroup d: warpgroup d's accumulators -> partial row sums ---
+        const int d = (warp - kWarpEpi0) >> 2, L = (warp & 3) * 32 + lane;
+        const int te = tid - kTidEpi0;  // 0 .. 255
         const uint32_t lane_off = tmem_lane_base(warp);
-        const uint32_t tA0 = tmem + wg * 128, tD0 = tmem + wg * 128 + 64;
-        const int gbytes = dec_b_group_bytes(N);
-        int item = 0, ua = 0, ud = 0;
-        bool okd = true;
-
-        // the up phase's digit operand: every token's x (vector v = token)
-        for (int i = tid; i < a.b_bytes / 16; i += kDecThreads)
-            reinterpret_cast<uint4*>(s_B)[i] = make_uint4(0u, 0u, 0u, 0u);
-        if (tid < a.M) S.vec_ptr[tid] = a.x + (size_t)tid * a.H;
-        bar_sync(kBarDec, kDecThreads);
-        if (!stopped) digitize_b<DT>(S.vec_ptr, a.M, a.H, N, T, s_B, s_fs, kDecThreads);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        bar_sync(kBarDec, kDecThreads);
-        dstamp(a, 4);
-
+        const uint32_t tD0 = tmem + d * 256 + 128;
+        int ude[2] = {0, 0}, uc = 0;
+        bool oke = true;
+        long long w_d = 0, cy_epi = 0;
+        const bool prof = a.trace != nullptr && te == 0;
+        {  // the up phase's digit operand: every token's x (vector v = token)
+            for (int i = te; i < a.b_bytes / 16; i += kDecEpiThreads)
+                reinterpret_cast<uint4*>(s_B)[i] = make_uint4(0u, 0u, 0u, 0u);
+            if (te < a.M) S.vec_ptr[te] = a.x + (size_t)te * a.H;
+            bar_sync(kBarEpi, kDecEpiThreads);
+            if (!stopped) digitize_b<DT>(S.vec_ptr, a.M, a.H, N, T, GP, s_B, s_fs, kDecEpiThreads, kTidEpi0);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            bar_sync(kBarEpi, kDecEpiThreads);
+            if (te == 0) {
+                dstamp_thread(a, 3);
+                mbar_arrive(&S.b_ready[0]);
+            }
+        }
         for (int ph = 0; ph < 2; ++ph) {
             const int nt = ph ? nt_dn : nt_up, nC = ph ? nC_dn : nC_up, nG = ph ? nG_dn : nG_up;
             const int4* tiles = ph ? S.tiles_dn : S.tiles_up;
-            const uint16_t* sc = ph ? a.s_dn : a.s_ug;
-            const uint16_t* bc = ph ? a.b_dn : a.b_ug;
-            const int Nrows = ph ? a.H : 2 * a.I;
-            const int nsb = (ph ? a.I : a.H) / GS;
             if (ph == 1) {
                 // act complete on every CTA: grid barrier, then the down phase's digits
                 __threadfence();
-                bar_sync(kBarDec, kDecThreads);
-                dstamp(a, 6);
-                if (tid == 0) {
+                bar_sync(kBarEpi, kDecEpiThreads);
+                if (te == 0) dstamp_thread(a, 6);
+                if (te == 0) {
                     // every CTA arrives (also after an error), so the counter returns to zero
                     const bool wait = !*abort_flag;
                     S.flag = grid_barrier_thread(reinterpret_cast<unsigned*>(a.ctrl + kCtrlArrive),
                                                  reinterpret_cast<unsigned*>(a.ctrl + kCtrlGen), a.spin_limit,
                                                  wait) && wait;
                 }
-                bar_sync(kBarDec, kDecThreads);
-                if (!S.flag) okd = false;
-                dstamp(a, 7);
-                if (okd) {
-                    for (int i = tid; i < a.b_bytes / 16; i += kDecThreads)
+                bar_sync(kBarEpi, kDecEpiThreads);
+                if (!S.flag) oke = false;
+                if (te == 0) dstamp_thread(a, 7);
+                if (oke && !stopped) {
+                    for (int i = te; i < a.b_bytes / 16; i += kDecEpiThreads)
                         reinterpret_cast<uint4*>(s_B)[i] = make_uint4(0u, 0u, 0u, 0u);
+                    bar_sync(kBarEpi, kDecEpiThreads);
+                    for (int us = 0; us < S.nudn; ++us) {
+                        const int4 un = S.units[S.udn0 + us];
+                        if (te < un.z) S.vec_ptr[te] = a.act + (size_t)S.sorted[un.y + te] * a.I;
+                        bar_sync(kBarEpi, kDecEpiThreads);
+                        // threads numbered from 0 within the epilogue warps
+                        digitize_b<DT>(S.vec_ptr, un.z, a.I, N, T, GP, s_B + (size_t)us * nG_dn * gbytes,
+                                       s_fs + (size_t)us * T * nG_dn, kDecEpiThreads, kTidEpi0);
+                        bar_sync(kBarEpi, kDecEpiThreads);
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 }
-                bar_sync(kBarDec, kDecThreads);
-                for (int us = 0; us < S.nudn && okd && !stopped; ++us) {
-                    const int4 un = S.units[S.udn0 + us];
-                    if (tid < un.z) S.vec_ptr[tid] = a.act + (size_t)S.sorted[un.y + tid] * a.I;
-                    bar_sync(kBarDec, kDecThreads);
-                    digitize_b<DT>(S.vec_ptr, un.z, a.I, N, T, s_B + (size_t)us * nG_dn * gbytes,
-                                   s_fs + (size_t)us * T * nG_dn, kDecThreads);
-                    bar_sync(kBarDec, kDecThreads);
+                bar_sync(kBarEpi, kDecEpiThreads);
+                if (te == 0) {
+                    dstamp_thread(a, 8);
+                    mbar_arrive(&S.b_ready[1]);
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                bar_sync(kBarDec, kDecThreads);
-                dstamp(a, 8);
             }
             for (int t = 0; t < nt; ++t) {
                 const int4 tl = tiles[t];
                 const int4 un = S.units[tl.x];
-                const int e = un.x;
-                // the thread's weight row: up rows in lanes [0, 64), gate rows in [64, 128)
-                const bool rvalid = ph ? (L < tl.z) : ((L & 63) < tl.z);
-                const int grow = ph ? tl.y + L : ((L < 64) ? tl.y + L : a.I + tl.y + (L - 64));
-                const size_t srow = ((size_t)e * Nrows + (rvalid ? grow : 0)) * nsb;
-                const uint16_t* srp = sc + srow;
-                const uint16_t* brp = bc + srow;
                 // vectors of this tile: up -- the unit's tokens; down -- its pairs
                 const int vmask = ph ? ((1 << un.z) - 1) : un.w;
                 const float2* fsb = ph ? s_fs + (size_t)(tl.x - S.udn0) * T * nG_dn : s_fs;
-                float acc[8];
+                float acc[T];
 #pragma unroll
-                for (int v = 0; v < 8; ++v) acc[v] = 0.f;
-                int nGw = 0;
-                for (int c = 0; c < nC; ++c) nGw += min(2, max(0, min(8, nG - 8 * c) - 2 * wg));
-                const int npk = (nGw + GP - 1) / GP;
-                const int item0 = item;
-                int pk_done = 0;  // packs of this tile whose epilogue ran
-                int q = 0;        // groups of this tile dequantised by the warpgroup
-
-                // epilogue of pack k of this tile (groups [k GP, min((k+1) GP, nGw)) of the warpgroup)
-                auto epilogue = [&](int k) {
-                    const int buf = ud % ND;
-                    if (okd) okd = mbar_wait_warp(&S.d_full[wg][buf], (ud / ND) & 1, a.spin_limit, abort_flag);
-                    ++ud;
-                    if (!okd) return;
-                    tc_after_sync();
-                    uint32_t d0[16], d1[16];
-                    tmem_ld16_nowait(tD0 + buf * N + lane_off, d0);
-                    if (N == 32) tmem_ld16_nowait(tD0 + buf * N + 16 + lane_off, d1);
-                    tmem_ld_wait();
-                    tc_before_sync();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&S.d_empty[wg][buf]);
-                    const int q0 = k * GP, q1 = min(q0 + GP, nGw);
+                for (int v = 0; v < T; ++v) acc[v] = 0.f;
+                for (int c = 0; c < nC; ++c) {
+                    if (wg_groups(nG, c, d) == 0) continue;
+                    const int sl = uc % kDecStash;
+                    if (oke) oke = mbar_wait_warp(&S.sb_full[d][sl], (uc / kDecStash) & 1, a.spin_limit, abort_flag);
+                    const uint4 sbw = oke ? s_stash[((size_t)d * kDecStash + sl) * 128 + L] : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-                    for (int gl = 0; gl < 4; ++gl) {
-                        const int qq = q0 + gl;
-                        if (gl >= GP || qq >= q1) continue;
-                        const int g = 8 * (qq >> 1) + 2 * wg + (qq & 1);
-                        // this group's scale and bias words (copied at its chunk's dequantisation)
-                        const int rp = ((item0 + (qq >> 1)) & 3) * 4 + wg;
-                        const uint32_t sw = s_sb[(rp * 2 + 0) * 128 + L], bw = s_sb[(rp * 2 + 1) * 128 + L];
-                        const int hs = (GS == 64) ? (qq & 1) : (wg & 1);
-                        const float s = Half<DT>::to_f((uint16_t)(sw >> (16 * hs)));
-                        const float b = Half<DT>::to_f((uint16_t)(bw >> (16 * hs)));
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const int iw = 2 * d + hh;
 #pragma unroll
-                        for (int v = 0; v < 8; ++v) {
-                            if (v < T && ((vmask >> v) & 1)) {
-                                const int nb = gl * 4 * T + v * 4;  // < 16 for T <= 4; < 32 for T = 8
-                                int D[4];
+                        for (int pk = 0; pk < 2 / GP; ++pk) {
+                            const int buf = ude[hh] % ND;
+                            const long long tw0 = a.trace ? gtime() : 0;
+                            if (oke) oke = mbar_wait_warp(&S.d_full[iw][buf], (ude[hh] / ND) & 1, a.spin_limit, abort_flag);
+                            if (a.trace) w_d += gtime() - tw0;
+                            ++ude[hh];
+                            const long long cy0 = prof ? clock64() : 0;
+                            if (oke) {
+                                tc_after_sync();
+                                uint32_t dv[N];
+                                const uint32_t taddr = tD0 + hh * 64 + buf * N + lane_off;
+                                if (N == 16) tmem_ld16_nowait(taddr, *reinterpret_cast<uint32_t(*)[16]>(dv));
+                                else tmem_ld32_nowait(taddr, *reinterpret_cast<uint32_t(*)[32]>(dv));
+                                tmem_ld_wait();
+                                tc_before_sync();
+                                __syncwarp();
+                                if (lane == 0) mbar_arrive(&S.d_empty[iw][buf]);
 #pragma unroll
-                                for (int dd = 0; dd < 4; ++dd) {
-                                    const int col = nb + dd;
-                                    D[dd] = (int)(col < 16 ? d0[col & 15] : d1[col & 15]);
-                                }
-                                const float f =
-                                    fmaf((float)D[0], 16777216.f, fmaf((float)D[1], 65536.f, (float)(D[2] * 256 + D[3])));
-                                const float2 fsv = fsb[v * nG + g];
-                                acc[v] += fmaf(s, f * fsv.x, b * fsv.y);
-                            }
-                        }
-                    }
-                };
-
-                for (int c = 0; c < nC; ++c, ++item) {
-                    const int s = item % S_;
-                    if (okd) okd = mbar_wait_warp(&S.full[s], (item / S_) & 1, a.spin_limit, abort_flag);
-                    const int cnt = min(2, max(0, min(8, nG - 8 * c) - 2 * wg));
-                    if (cnt > 0 && okd) {
-                        // scale and bias words of the chunk's two groups, for the epilogue
-                        {
-                            const int rp = (item & 3) * 4 + wg;
-                            const int gw = (GS == 64) ? 8 * c + 2 * wg : ((8 * c + 2 * wg) / 2) & ~1;
-                            cp_async4(smem_u32(s_sb + (rp * 2 + 0) * 128 + L), srp + gw, rvalid);
-                            cp_async4(smem_u32(s_sb + (rp * 2 + 1) * 128 + L), brp + gw, rvalid);
-                        }
-                        const unsigned char* row = s_ring + (size_t)s * kDecStageBytes + L * 128;
-                        uint4 raw[2];
+                                for (int gl = 0; gl < GP; ++gl) {
+                                    const int j = 2 * hh + pk * GP + gl;  // group of the warpgroup's four
+                                    const int g = 8 * c + 4 * d + j;
+                                    float sf, bf;
+                                    if (GS == 64) {
+                                        const uint32_t sw = (j < 2) ? sbw.x : sbw.y, bw = (j < 2) ? sbw.z : sbw.w;
+                                        sf = Half<DT>::to_f((uint16_t)(sw >> (16 * (j & 1))));
+                                        bf = Half<DT>::to_f((uint16_t)(bw >> (16 * (j & 1))));
+                                    } else {
+                                        sf = Half<DT>::to_f((uint16_t)(sbw.x >> (16 * (j >> 1))));
+                                        bf = Half<DT>::to_f((uint16_t)(sbw.z >> (16 * (j >> 1))));
+                                    }
 #pragma unroll
-                        for (int tt = 0; tt < 2; ++tt)
-                            raw[tt] = tt < cnt ? *reinterpret_cast<const uint4*>(row + (((2 * wg + tt) ^ (L & 7)) << 4))
-                                               : make_uint4(0u, 0u, 0u, 0u);
-                        const int slot = ua & 1;
-                        if (ua >= 2) okd = mbar_wait_warp(&S.a_empty[wg][slot], ((ua - 2) >> 1) & 1, a.spin_limit, abort_flag);
-                        if (okd) {
-                            tc_after_sync();
-#pragma unroll
-                            for (int tt = 0; tt < 2; ++tt) {
-                                if (tt < cnt) {
-                                    const uint32_t wv[4] = {raw[tt].x, raw[tt].y, raw[tt].z, raw[tt].w};
-                                    uint32_t m[16];
-#pragma unroll
-                                    for (int p = 0; p < 4; ++p)
-#pragma unroll
-                                        for (int i = 0; i < 4; ++i) m[4 * p + i] = wv[i] & (0x03030303u << (2 * p));
-                                    tmem_st16(tA0 + slot * 32 + tt * 16 + lane_off, m);
+                                    for (int v = 0; v < T; ++v) {
+                                        if ((vmask >> v) & 1) {
+                                            const int nb = gl * 4 * T + v * 4;
+                                            const float f = fmaf((float)(int)dv[nb], 16777216.f,
+                                                                 fmaf((float)(int)dv[nb + 1], 65536.f,
+                                                                      (float)((int)dv[nb + 2] * 256 + (int)dv[nb + 3])));
+                                            const float2 fsv = fsb[v * nG + g];
+                                            acc[v] += fmaf(sf, f * fsv.x, bf * fsv.y);
+                                        }
+                                    }
                                 }
                             }
-                            tmem_st_wait();
-                            tc_before_sync();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&S.a_full[wg][slot]);
+                            if (prof) cy_epi += clock64() - cy0;
                         }
-                        ++ua;
                     }
-                    cp_async_commit();
-                    q += cnt;
                     __syncwarp();
-                    if (lane == 0 && okd) mbar_arrive(&S.empty[s]);
-                    // packs closed before this chunk's groups: their MMAs were issued already
-                    const int closed = (q - cnt) / GP;
-                    if (pk_done < closed) cp_async_wait<1>();
-                    while (pk_done < closed) epilogue(pk_done++);
+                    if (lane == 0 && oke) mbar_arrive(&S.sb_empty[d][sl]);
+                    ++uc;
                 }
-                cp_async_wait<0>();
-                while (pk_done < npk) epilogue(pk_done++);
-                // ---- tile end: warpgroup partials -> ((w0 + w1) + (w2 + w3)) ------
-                // (the partials reuse the scale/bias buffer: no copy is in flight now)
-                bar_sync(kBarDec, kDecThreads);
+                // ---- tile end: warpgroup partials -> (e0 + e1) -----------------------
 #pragma unroll
-                for (int v = 0; v < 8; ++v)
-                    if (v < T && ((vmask >> v) & 1)) s_red[((size_t)wg * T + v) * 128 + L] = acc[v];
-                bar_sync(kBarDec, kDecThreads);
-                if (okd) {
+                for (int v = 0; v < T; ++v)
+                    if ((vmask >> v) & 1) s_red[((size_t)d * T + v) * 128 + L] = acc[v];
+                bar_sync(kBarEpi, kDecEpiThreads);
+                if (oke) {
                     const size_t st = (size_t)T * 128;
                     auto red_sum = [&](int v, int l) {
                         const float* r = s_red + (size_t)v * 128 + l;
-                        return (r[0] + r[st]) + (r[2 * st] + r[3 * st]);
+                        return r[0] + r[st];
                     };
                     if (ph == 0) {
-                        for (int i = tid; i < un.z * 64; i += kDecThreads) {
+                        for (int i = te; i < un.z * 64; i += kDecEpiThreads) {
                             const int j = i >> 6, l = i & 63;
                             if (l >= tl.z) continue;
                             const int pr = S.sorted[un.y + j];
@@ -758,7 +902,7 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                                 swiglu_staged<DT>(red_sum(m, l), red_sum(m, l + 64), a.clamp);
                         }
                     } else {
-                        for (int i = tid; i < un.z * 128; i += kDecThreads) {
+                        for (int i = te; i < un.z * 128; i += kDecEpiThreads) {
                             const int j = i >> 7, l = i & 127;
                             if (l >= tl.z) continue;
                             const int pr = S.sorted[un.y + j];
@@ -766,24 +910,24 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                         }
                     }
                 }
-                bar_sync(kBarDec, kDecThreads);
+                bar_sync(kBarEpi, kDecEpiThreads);
             }
-            if (ph == 0) dstamp(a, 5);
+            if (ph == 0 && te == 0) dstamp_thread(a, 5);
         }
         // a warp that gave up makes the others give up at their next wait
-        if (!okd) *abort_flag = 1;
-        bar_sync(kBarDec, kDecThreads);
+        if (!oke) *abort_flag = 1;
+        bar_sync(kBarEpi, kDecEpiThreads);
         const bool all_ok = !*abort_flag;
-        if (!all_ok && tid == 0) atomicExch(a.ctrl + kCtrlError, MOMIJ_ERR_TIMEOUT);
-        dstamp(a, 9);
+        if (!all_ok && te == 0) atomicExch(a.ctrl + kCtrlError, MOMIJ_ERR_TIMEOUT);
+        if (te == 0) dstamp_thread(a, 9);
 
         // ---- last-arriver combine per 64-row block --------------------------------
         // (the counts are added also after an error or a stop, so that every
         // counter returns to zero; the status word then flags the output)
         {
             __threadfence();  // down rows written by this thread, before the block counters
-            bar_sync(kBarDec, kDecThreads);
-            if (tid == 0) {
+            bar_sync(kBarEpi, kDecEpiThreads);
+            if (te == 0) {
                 int ns = 0;
                 for (int t = 0; t < nt_dn_all; ++t) {
                     const int4 tl = S.tiles_dn[t];
@@ -796,19 +940,19 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                 S.nseg = ns;
                 S.nlast = 0;
             }
-            bar_sync(kBarDec, kDecThreads);
-            if (tid < S.nseg) {
-                const int2 sg = S.seg[tid];
+            bar_sync(kBarEpi, kDecEpiThreads);
+            if (te < S.nseg) {
+                const int2 sg = S.seg[te];
                 const int bs = sg.x * 64, be = min(a.H, bs + 64);
                 const unsigned target = (unsigned)U * (unsigned)(be - bs);
                 const unsigned old = atomicAdd(a.block_ctr + sg.x, (unsigned)sg.y);
                 if (old + (unsigned)sg.y == target) S.last[atomicAdd(&S.nlast, 1)] = sg.x;
             }
-            bar_sync(kBarDec, kDecThreads);
+            bar_sync(kBarEpi, kDecEpiThreads);
             const int nlast = S.nlast;
             if (nlast) {
                 __threadfence();
-                for (int it = tid; it < nlast * a.M * 64; it += kDecThreads) {
+                for (int it = te; it < nlast * a.M * 64; it += kDecEpiThreads) {
                     const int qb = it / (a.M * 64), rem = it % (a.M * 64);
                     const int m = rem / 64, r = rem % 64;
                     const int n = S.last[qb] * 64 + r;
@@ -833,10 +977,14 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                         if (all_ok && !stopped) a.y[off] = Half<DT>::from_f(accv);
                     }
                 }
-                if (tid < nlast) a.block_ctr[S.last[tid]] = 0u;  // ready for the next call
+                if (te < nlast) a.block_ctr[S.last[te]] = 0u;  // ready for the next call
             }
         }
-        dstamp(a, 10);
+        if (te == 0) {
+            dstamp_thread(a, 10);
+            dwait_put(a, 17, w_d);
+            dwait_put(a, 18, cy_epi);
+        }
     }
     tc_before_sync();
     __syncthreads();

@@ -14,34 +14,50 @@ namespace momij {
 // wait that gave up), [3] grid-barrier arrivals, [4] grid-barrier generation.
 constexpr int kCtrlStatus = 1, kCtrlError = 2, kCtrlArrive = 3, kCtrlGen = 4;
 
-constexpr int kDecWarps = 16;             // dequantise + epilogue: 4 warpgroups of 4 warps
-constexpr int kDecThreads = 32 * kDecWarps;
-constexpr int kDecProducers = 2;          // TMA-issuing warps (lane 0 each), alternate stages
-constexpr int kDecThreadsAll = kDecThreads + 32 * (kDecProducers + 1);  // + the MMA-issuing warp
-constexpr int kDecStageBytes = 128 * 128;  // one (tile, 128-byte K chunk): 128 rows x 128 B
+// Warp roles of the decode kernel (20 warps):
+//   0-7   dequantise: warpgroup d (warps 4d..4d+3) turns the 16-code words of
+//         groups [4d, 4d+4) of every stage into the MMA's A operand in TMEM;
+//   8-15  epilogue: warpgroup d (warps 8+4d..) reads warpgroup d's
+//         accumulators (tcgen05.ld), applies scales and biases, writes outputs;
+//   16-19 MMA issue (lane 0): warp 16+2d+h issues the MMAs of groups 2h, 2h+1
+//         of warpgroup d's four (a thread issues one MMA per ~60 cycles, and
+//         the issue rate grows with the number of issuing warps);
+//   20-21 TMA producers (lane 0), alternate stages.
+constexpr int kDecDeqWarps = 8;
+constexpr int kDecEpiWarps = 8;
+constexpr int kDecMmaWarps = 4;
+constexpr int kDecProducers = 2;
+constexpr int kDecThreadsAll = 32 * (kDecDeqWarps + kDecEpiWarps + kDecMmaWarps + kDecProducers);
+constexpr int kDecEpiThreads = 32 * kDecEpiWarps;
+constexpr int kDecRouteThreads = 32 * (kDecMmaWarps + kDecProducers);  // route while the others encode x
+constexpr int kDecCodeBytes = 128 * 128;   // a stage's codes: 128 rows x one 128-byte K chunk (8 groups)
+constexpr int kDecSbBytes = 128 * 16;      // a stage's scales (and again biases): 128 rows x 16 B
+constexpr int kDecStageBytes = kDecCodeBytes + 2 * kDecSbBytes;  // 20 KB, a multiple of 1 KB
 constexpr int kDecMaxStages = 12;
 constexpr int kDecMaxTiles = 48;           // tiles per phase per CTA (host-checked bound)
 constexpr int kDecMaxPairs = 64;           // M * K
 constexpr int kDecMaxLastBlocks = 64;      // (unit, 64-row block) segments per CTA in the combine
-constexpr int kDecBoxes = 4;               // TMA box heights 64, 32, 16, 8 rows
+constexpr int kDecAslots = 2;              // A slots per warpgroup (64 TMEM columns each)
+constexpr int kDecStash = 4;               // scale/bias stash slots per warpgroup (chunks)
 constexpr int kDecTmemCols = 512;
-constexpr int kTracePointsDec = 16;
+constexpr int kTracePointsDec = 32;
+// TMA maps: 2D over [rows, row bytes] with box heights 64, 16, 8 (index 0..2),
+// a box of 128 rows (index 3, down projection), and a 3D map whose box takes
+// 64 rows of both the up and the gate half (index 4, up||gate).
+constexpr int kDecMaps = 5;
 
 struct DecodeArgs {
-    // TMA maps over the packed codes viewed as bytes [E * N rows, Kd / 4],
-    // 128-byte swizzle, box 128 B x {64, 32, 16, 8} rows.
-    CUtensorMap map_ug[kDecBoxes];
-    CUtensorMap map_dn[kDecBoxes];
+    // codes / scales / biases of the up||gate and the down projection, as
+    // bytes [E * N rows, row bytes]: codes with 128-byte swizzle (box 128 B x
+    // rows), scales and biases without (box 16 B x rows)
+    CUtensorMap map_ug[kDecMaps], map_sug[kDecMaps], map_bug[kDecMaps];
+    CUtensorMap map_dn[kDecMaps], map_sdn[kDecMaps], map_bdn[kDecMaps];
     const float* logits;     // [M, E] or nullptr (then inds_in / scores_in)
     const int32_t* inds_in;  // [M, K]
     const float* scores_in;
     int32_t* inds_out;       // optional copies of the routing (CTA 0 writes)
     float* scores_out;
     const uint16_t* x;       // [M, H]
-    const uint16_t* s_ug;    // [E, 2I, H/gs]
-    const uint16_t* b_ug;
-    const uint16_t* s_dn;    // [E, H, I/gs]
-    const uint16_t* b_dn;
     uint16_t* act;           // [M*K, I] staged SwiGLU output
     uint16_t* down;          // [M*K, H] staged down-projection output
     uint16_t* y;             // [M, H] output, or nullptr when h is set
@@ -56,7 +72,7 @@ struct DecodeArgs {
     int spin_limit;          // polls of a bounded wait before it gives up
     float clamp;
     // dynamic shared-memory carve-up (byte offsets from the 1024-aligned base)
-    int off_ring, off_b, off_fs, off_sb, off_logits;
+    int off_ring, off_b, off_fs, off_stash, off_red, off_logits, off_keys;
     int b_bytes;             // bytes of the B region
 };
 
@@ -66,6 +82,9 @@ __global__ void moe_decode_kernel(const __grid_constant__ DecodeArgs a);
 
 // MMA N of a column set of T vectors x 4 digits (M = 128 needs N % 16 == 0).
 __host__ __device__ constexpr int dec_mma_n(int T) { return T <= 4 ? 16 : 4 * T; }
+// Groups sharing one accumulator pack (their column sets side by side): as
+// many as fit in N, at most the two groups one issuing warp takes per chunk.
+__host__ __device__ constexpr int dec_gp(int T) { return (dec_mma_n(T) / (4 * T)) < 2 ? 1 : 2; }
 
 // Bytes of B (digit operand) per group: two MMAs of N rows x 32 K-bytes.
 __host__ __device__ constexpr int dec_b_group_bytes(int N) { return 64 * N; }

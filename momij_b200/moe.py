@@ -23,7 +23,7 @@ import re
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "lib", "libmomij_moe.so")
+LIB_PATH = os.environ.get("MOMIJ_LIB_PATH") or os.path.join(HERE, "lib", "libmomij_moe.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "momij_moe.h")
 
 OK, UNSUPPORTED_SHAPE, NOT_READY, NO_DEVICE, INVALID_ARGUMENT = 0, 1, 2, 3, 4
