@@ -17,6 +17,7 @@
 #include "kernels.cuh"
 #include "gemv_core.cuh"
 #include "decode.cuh"
+#include "layer.cuh"
 #include "prefill.cuh"
 
 using namespace momij;
@@ -336,10 +337,10 @@ bool fused_enabled() {
 // Static shared memory of the decode kernel (DecShared and the kernel's own).
 constexpr int kDecStaticReserve = 8192;
 
-// Launches the whole layer as one cooperative kernel when the batch is a
-// decode/verify batch that fits; kNotApplicable lets the caller fall back to
-// the multi-kernel path.
-int run_fused_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, cudaStream_t st) {
+// Launches the whole layer of a 2..8-token batch (or, with MOMIJ_DECODE_M1=tc,
+// one token) as one cooperative tcgen05 kernel (decode.cu) when it fits;
+// kNotApplicable lets the caller fall back.
+int run_decode_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, cudaStream_t st) {
     const int P = c.M * c.K;
     if (!fused_enabled() || c.M > 8 || P > kDecMaxPairs || c.E > 256 || c.K > 32 || c.H % 512 || c.I % 512)
         return kNotApplicable;
@@ -390,15 +391,14 @@ int run_fused_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, 
     a.clamp = c.clamp;
 
     // shared memory: ring of stages (codes + scales + biases) | B | per-group
-    // factors | scale/bias stash | tile-end partials; the logits and router
+    // factors | tile-end partials; the logits and router
     // keys live in the ring (the producers start only after the routing)
     const size_t b_bytes = (size_t)std::max(nG_up, 2 * nG_dn) * dec_b_group_bytes(N);
     const size_t fs_bytes = align_up(8 * (size_t)std::max(c.M * nG_up, 2 * T * nG_dn), 16);
-    const size_t stash_bytes = (size_t)2 * kDecStash * 128 * 16;
     const size_t red_bytes = (size_t)2 * T * 128 * 4;
     const size_t lg_bytes = align_up(4 * (size_t)(c.logits ? c.M * c.E : 0), 16);
     const size_t key_bytes = align_up(8 * (size_t)(c.logits ? c.M * c.E : 0), 16);
-    const size_t fixed = align_up(b_bytes, 1024) + fs_bytes + stash_bytes + red_bytes + 1024;
+    const size_t fixed = align_up(b_bytes, 1024) + fs_bytes + red_bytes + 1024;
     int optin = 0, dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
@@ -409,7 +409,6 @@ int run_fused_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, 
     a.off_ring = (int)off; off += (size_t)stages * kDecStageBytes;
     a.off_b = (int)off; off += align_up(b_bytes, 1024);
     a.off_fs = (int)off; off += fs_bytes;
-    a.off_stash = (int)off; off += stash_bytes;
     a.off_red = (int)off; off += red_bytes;
     a.off_logits = a.off_ring;
     a.off_keys = a.off_ring + (int)lg_bytes;
@@ -447,6 +446,168 @@ int run_fused_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, 
     }
     prof_end(slot, st);
     return cuda_status(e);
+}
+
+// ---- single-token layer engine (layer.cu) ----------------------------------
+using LayerFn = void (*)(const LayerArgs);
+
+LayerFn pick_layer(int dtype, int gs) {
+    if (dtype == MOMIJ_DTYPE_BF16)
+        return gs == 64 ? moe_layer_kernel<MOMIJ_DTYPE_BF16, 64, 1, layer_stages(1)>
+                        : moe_layer_kernel<MOMIJ_DTYPE_BF16, 128, 1, layer_stages(1)>;
+    return gs == 64 ? moe_layer_kernel<MOMIJ_DTYPE_F16, 64, 1, layer_stages(1)>
+                    : moe_layer_kernel<MOMIJ_DTYPE_F16, 128, 1, layer_stages(1)>;
+}
+
+// One token's whole layer as one cooperative kernel on the warp-level engine
+// (the fastest single-token path measured); kNotApplicable when it does not fit.
+int run_layer_engine(const LayerCall& c, int dtype, int gs, const Workspace& ws, cudaStream_t st) {
+    const int P = c.M * c.K;
+    if (c.M != 1 || P > kLayerMaxPairs || c.E > 1024 || c.K > 32) return kNotApplicable;
+    const int tmax = 1, stages = layer_stages(tmax), rt = item_tiles(tmax);
+    const int G = current_device_sm_count();
+    if (G <= 0) return kNotApplicable;
+    LayerArgs a{};
+    a.logits = c.logits;
+    a.inds_in = c.inds_in;
+    a.scores_in = c.scores_in;
+    a.inds_out = c.inds_out;
+    a.scores_out = c.scores_out;
+    a.x = static_cast<const uint16_t*>(c.x);
+    a.w_ug = c.w_ug;
+    a.s_ug = static_cast<const uint16_t*>(c.s_ug);
+    a.b_ug = static_cast<const uint16_t*>(c.b_ug);
+    a.w_dn = c.w_dn;
+    a.s_dn = static_cast<const uint16_t*>(c.s_dn);
+    a.b_dn = static_cast<const uint16_t*>(c.b_dn);
+    a.y = c.resid_h ? nullptr : static_cast<uint16_t*>(c.y);
+    a.h = static_cast<uint16_t*>(c.resid_h);
+    a.M = c.M;
+    a.H = c.H;
+    a.I = c.I;
+    a.E = c.E;
+    a.K = c.K;
+    a.clamp = c.clamp;
+    a.stop = g_stop_flag.load();
+    a.spin_limit = spin_limit();
+    a.nK_up = a.H / kChunk;
+    a.nK_dn = a.I / kChunk;
+    const long long rows_up = ((long long)P * a.I + G - 1) / G;
+    const long long rows_dn = ((long long)P * a.H + G - 1) / G;
+    const int mu_up = (int)std::min<long long>(P, rows_up / a.I + 2);
+    const int mu_dn = (int)std::min<long long>(P, rows_dn / a.H + 2);
+    const int mt_up = (int)(rows_up / 8 + mu_up + 1);
+    const int mt_dn = (int)(rows_dn / 16 + mu_dn + 1);
+    if (rows_dn / 64 + 2 * mu_dn > kLayerMaxLastBlocks) return kNotApplicable;
+    const int max_units = std::max(mu_up, mu_dn), max_tiles = std::max(mt_up, mt_dn);
+    const int vec_dn = std::min(P, mu_dn * tmax);
+    a.max_tiles = max_tiles;
+    a.max_units = max_units;
+    a.max_vec = vec_dn;
+    const size_t ndg = std::max((size_t)a.M * (a.H / 64), (size_t)vec_dn * (a.I / 64));
+    const size_t limit = (size_t)max_dyn_smem();
+    size_t off = 0;
+    a.off_logits = (int)off; off += a.logits ? 4 * (size_t)a.M * a.E : 0;
+    off = align_up(off, 16);
+    a.off_keys = (int)off; off += a.logits ? 8 * (size_t)a.M * a.E : 0;
+    a.off_inds = (int)off; off += 4 * (size_t)P;
+    a.off_scores = (int)off; off += 4 * (size_t)P;
+    a.off_sorted = (int)off; off += 4 * (size_t)P;
+    off = align_up(off, 16);
+    a.off_pflag = (int)off; off += 16 * (size_t)P;  // per sorted pair: (expert, before, count)
+    a.off_units = (int)off; off += 16 * (size_t)P;
+    a.off_tiles_up = (int)off; off += 16 * (size_t)max_tiles;
+    a.off_lunits_up = (int)off; off += 16 * (size_t)max_units;
+    a.off_seg_up = (int)off; off += 16 * (size_t)max_units;
+    a.off_tiles_dn = (int)off; off += 16 * (size_t)max_tiles;
+    a.off_lunits_dn = (int)off; off += 16 * (size_t)max_units;
+    a.off_seg_dn = (int)off; off += 16 * (size_t)max_units;
+    a.off_upair_up = (int)off; off += 4 * (size_t)max_units * tmax;
+    a.off_uslot_up = (int)off; off += 4 * (size_t)max_units * tmax;
+    a.off_upair_dn = (int)off; off += 4 * (size_t)max_units * tmax;
+    a.off_uslot_dn = (int)off; off += 4 * (size_t)max_units * tmax;
+    a.off_xvecs = (int)off; off += 4 * (size_t)a.M;
+    a.off_vecs_dn = (int)off; off += 4 * (size_t)vec_dn;
+    off = align_up(off, 16);
+    a.off_fs = (int)off; off += 8 * ndg;
+    off = align_up(off, 16);
+    a.off_dig = (int)off; off += (size_t)kDgStride * ndg;
+    off = align_up(off, 16);
+    // the red and scale/bias buffers take what the ring leaves, up to a whole
+    // phase per batch; the phases share them
+    const size_t ring = (size_t)kConsumerWarps * stages * slot_bytes(tmax);
+    if (off + ring + 256 > limit) return kNotApplicable;
+    const size_t avail = limit - off - ring - 256;
+    const size_t rpt_up = 4 * (size_t)((a.nK_up + 1) / 2) * tmax * red_row(tmax),
+                 rpt_dn = 4 * (size_t)((a.nK_dn + 1) / 2) * tmax * red_row(tmax);
+    const size_t spt_up = sb_bytes_per_tile(a.H, gs, true), spt_dn = sb_bytes_per_tile(a.I, gs, true);
+    size_t bu = (size_t)(mt_up + rt - 1) / rt * rt, bd = (size_t)(mt_dn + rt - 1) / rt * rt;
+    auto need = [&]() { return std::max(bu * rpt_up, bd * rpt_dn) + std::max(bu * spt_up, bd * spt_dn) + 16; };
+    while (need() > avail && (bu > (size_t)rt || bd > (size_t)rt)) {
+        if (bu * (rpt_up + spt_up) >= bd * (rpt_dn + spt_dn) && bu > (size_t)rt)
+            bu = std::max((size_t)rt, (bu / 2 + rt - 1) / rt * rt);
+        else
+            bd = std::max((size_t)rt, (bd / 2 + rt - 1) / rt * rt);
+    }
+    if (need() > avail) return kNotApplicable;
+    a.batch_up = (int)bu;
+    a.batch_dn = (int)bd;
+    a.off_red = (int)off; off += std::max(bu * rpt_up, bd * rpt_dn);
+    off = align_up(off, 16);
+    a.off_sb = (int)off; off += std::max(bu * spt_up, bd * spt_dn);
+    off = align_up(off, 128);
+    a.off_stage = (int)off; off += ring;
+    LayerFn fn = pick_layer(dtype, gs);
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)off) != cudaSuccess)
+        return MOMIJ_ERR_CUDA;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kLayerThreads, off) != cudaSuccess || per_sm < 1)
+        return kNotApplicable;
+    a.trace = next_trace_slot(G);
+    a.ctrl = ws.plan;
+    a.block_ctr = ws.block_ctr;
+    a.act = ws.act;
+    a.down = ws.down;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(kLayerThreads);
+    cfg.dynamicSmemBytes = off;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    static bool pdl_with_coop = true;  // dropped if the driver refuses the pair
+    cfg.numAttrs = (pdl_enabled() && pdl_with_coop) ? 2 : 1;
+    const int slot = prof_begin(MOMIJ_KERNEL_LAYER, st);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a);
+    if (e != cudaSuccess && cfg.numAttrs == 2) {
+        cudaGetLastError();
+        pdl_with_coop = false;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, fn, a);
+    }
+    prof_end(slot, st);
+    return cuda_status(e);
+}
+
+bool m1_on_tcgen05() {
+    const char* v = std::getenv("MOMIJ_DECODE_M1");
+    return v && std::strcmp(v, "tc") == 0;
+}
+
+// The fused layer: one token on the warp-level engine, 2..8 tokens on the
+// tcgen05 kernel; kNotApplicable lets the caller fall back to the
+// multi-kernel path.
+int run_fused_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, cudaStream_t st) {
+    if (!fused_enabled()) return kNotApplicable;
+    if (c.M == 1 && !m1_on_tcgen05()) {
+        const int rc = run_layer_engine(c, dtype, gs, ws, st);
+        if (rc != kNotApplicable) return rc;
+    }
+    return run_decode_layer(c, dtype, gs, ws, st);
 }
 
 // ---- gather-GEMV dispatch --------------------------------------------------

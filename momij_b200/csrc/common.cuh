@@ -176,6 +176,36 @@ __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;\n" ::);
 }
 
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid barrier over gridDim.x co-resident CTAs by one thread: an arrival
+// counter that the last arriver resets, and a generation word it then
+// increments; the others wait for the generation to change.  The counter
+// never exceeds the grid size and the generation is compared for change only,
+// so neither wraps into a wrong state.  Every CTA arrives even when it later
+// gives up waiting, so the counter is back at zero after every call.
+__device__ inline bool grid_barrier_thread(unsigned* arrive, unsigned* gen, int limit, bool wait) {
+    __threadfence();
+    const unsigned g0 = ld_acquire_u32(gen);
+    const unsigned old = atomicAdd(arrive, 1u);
+    if (old == gridDim.x - 1) {
+        atomicExch(arrive, 0u);
+        __threadfence();
+        atomicAdd(gen, 1u);
+        return true;
+    }
+    if (!wait) return false;
+    for (int it = 0; it < limit; ++it) {
+        if (ld_acquire_u32(gen) != g0) return true;
+        __nanosleep(64);
+    }
+    return ld_acquire_u32(gen) != g0;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

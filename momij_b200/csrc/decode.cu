@@ -39,7 +39,6 @@ namespace {
 
 constexpr int kBarDec = 1;         // named barrier of the 512 dequantising threads
 constexpr int kDrainLimit = 1 << 24;  // polls while draining copies / MMAs on an error path
-constexpr int kGridSpinNs = 64;
 
 __device__ __forceinline__ void dstamp_thread(const DecodeArgs& a, int i) {
     if (a.trace) {
@@ -62,56 +61,6 @@ __device__ __forceinline__ void dwait_put(const DecodeArgs& a, int i, long long 
     if (a.trace) a.trace[(size_t)blockIdx.x * kTracePointsDec + i] = ns;
 }
 
-__device__ __forceinline__ int ld_acquire_shared(const volatile int* p) {
-    int v;
-    asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_u32((const void*)p)) : "memory");
-    return v;
-}
-__device__ __forceinline__ void red_release_add_shared(int* p, int v) {
-    asm volatile("red.release.cta.shared::cta.add.s32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Grid barrier over gridDim.x co-resident CTAs by one thread: an arrival
-// counter that the last arriver resets, and a generation word it then
-// increments; the others wait for the generation to change.  The counter
-// never exceeds the grid size and the generation is compared for change only,
-// so neither wraps into a wrong state.  Every CTA arrives even when it later
-// gives up waiting, so the counter is back at zero after every call.
-__device__ bool grid_barrier_thread(unsigned* arrive, unsigned* gen, int limit, bool wait) {
-    __threadfence();
-    const unsigned g0 = ld_acquire_u32(gen);
-    const unsigned old = atomicAdd(arrive, 1u);
-    if (old == gridDim.x - 1) {
-        atomicExch(arrive, 0u);
-        __threadfence();
-        atomicAdd(gen, 1u);
-        return true;
-    }
-    if (!wait) return false;
-    for (int it = 0; it < limit; ++it) {
-        if (ld_acquire_u32(gen) != g0) return true;
-        __nanosleep(kGridSpinNs);
-    }
-    return ld_acquire_u32(gen) != g0;
-}
-
-// ---- routing ---------------------------------------------------------------
-// Order of two candidates of the reference's reduction tree (see
-// route_topk_tree): a larger value wins; equal values (signed zeros compare
-// equal) go to the expert whose bit-reversed index (over the tree's width) is
-// smaller.  `rb` is the bit count of the width (8 for E <= 256).
-__device__ __forceinline__ uint32_t route_value_key(float v) {
-    uint32_t u = __float_as_uint(v);
-    if ((u & 0x7fffffffu) == 0) u = 0;  // -0 == +0
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ uint32_t rev_index(int e, int rb) { return __brev((uint32_t)e) >> (32 - rb); }
 
 // ---- work plan ------------------------------------------------------------
 // Sort the P <= 64 pairs by (expert, pair) and cut each expert's run into
@@ -285,53 +234,6 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
 }
 
 
-// Router of the M tokens by the `nthr` threads from thread `t0` (a named
-// barrier `bar` over them): 64-bit keys (value order, then the reference's
-// tree order on ties: the smaller bit-reversed index) in shared memory, then
-// candidate (m, e) lands at position #{e' : key(e') > key(e)} when that is
-// below K.  Tokens with a NaN logit take the reference's tree step by step
-// (route_topk_tree).  Scores: route_scores_warp.
-__device__ void route_tokens(const float* s_logits, unsigned long long* s_keys, const int* s_nan, int M,
-                             int E, int K, int t0, int nthr, int bar, int* s_inds, float* s_scores,
-                             long long* trace = nullptr) {
-    const int t = threadIdx.x - t0;
-    const int rb = 31 - __clz(route_tree_width(E));
-    for (int c = t; c < M * E; c += nthr) {
-        const int e = c % E;
-        s_keys[c] = ((unsigned long long)route_value_key(s_logits[c]) << 32) |
-                    (unsigned long long)(0xffffffffu - rev_index(e, rb));
-    }
-    bar_sync(bar, nthr);
-    constexpr int kParts = 8;  // threads per candidate
-    for (int base = 0; base < M * E * kParts; base += nthr) {
-        const int it = base + t;
-        const int c = it / kParts, sub = it % kParts;
-        int r = 0;
-        const bool valid = c < M * E;
-        const int m = valid ? c / E : 0;
-        if (valid && !s_nan[m]) {
-            const unsigned long long kc = s_keys[c];
-            const unsigned long long* kr = s_keys + m * E;
-#pragma unroll 8
-            for (int j = sub; j < E; j += kParts) r += kr[j] > kc;
-        }
-#pragma unroll
-        for (int o = 1; o < kParts; o <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
-        if (valid && sub == 0 && !s_nan[m] && r < K) s_inds[m * K + r] = c - m * E;
-    }
-    const int w = t >> 5, nw = nthr >> 5;
-    for (int m = w; m < M; m += nw)
-        if (s_nan[m]) route_topk_tree<8>(s_logits + m * E, E, K, s_inds + m * K);
-    bar_sync(bar, nthr);
-    if (trace && t == 0) {
-        unsigned long long tt;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tt));
-        trace[(size_t)blockIdx.x * kTracePointsDec + 25] = (long long)tt;
-    }
-    for (int m = w; m < M; m += nw) route_scores_warp(s_logits + m * E, E, K, s_inds + m * K, s_scores + m * K);
-}
-
-
 struct DecShared {
     int inds[kDecMaxPairs];
     float scores[kDecMaxPairs];
@@ -348,15 +250,10 @@ struct DecShared {
     uint32_t tmem;
     alignas(8) uint64_t full[kDecMaxStages];
     alignas(8) uint64_t empty[kDecMaxStages];
-    // per (warpgroup, A slot): warps of the warpgroup that wrote the slot, over all its
-    // uses (a warp reaches a slot's next use only after its previous MMAs completed,
-    // which needed all four warps' previous writes: the count cannot run ahead)
-    int a_ready[2][kDecAslots];
-    alignas(8) uint64_t a_empty[2][kDecAslots][2];  // [warpgroup][slot][issuing warp]
-    alignas(8) uint64_t d_full[4][4];                // [issuing warp][pack buffer]
+    alignas(8) uint64_t a_full[2][kDecAslots];   // [warpgroup][slot]: its four warps wrote the slot
+    alignas(8) uint64_t a_empty[2][kDecAslots];  // [warpgroup][slot]: both issuing warps commit
+    alignas(8) uint64_t d_full[4][4];             // [issuing warp][pack buffer]
     alignas(8) uint64_t d_empty[4][4];
-    alignas(8) uint64_t sb_full[2][kDecStash];
-    alignas(8) uint64_t sb_empty[2][kDecStash];
     alignas(8) uint64_t b_ready[2];
     alignas(8) uint64_t drain[4];
 };
@@ -385,16 +282,11 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
     if (tid == 0) {
         for (int s = 0; s < a.stages; ++s) {
             mbar_init(&S.full[s], 1);
-            mbar_init(&S.empty[s], kDecDeqWarps);
+            mbar_init(&S.empty[s], kDecDeqWarps + kDecEpiWarps);  // codes read; scales and biases read
         }
         for (int d = 0; d < 2; ++d) {
-            for (int s = 0; s < kDecAslots; ++s) S.a_ready[d][s] = 0;
-            for (int s = 0; s < kDecAslots; ++s)
-                for (int h = 0; h < 2; ++h) mbar_init(&S.a_empty[d][s][h], 1);
-            for (int s = 0; s < kDecStash; ++s) {
-                mbar_init(&S.sb_full[d][s], 4);
-                mbar_init(&S.sb_empty[d][s], 4);
-            }
+            for (int s = 0; s < kDecAslots; ++s) mbar_init(&S.a_full[d][s], 4);
+            for (int s = 0; s < kDecAslots; ++s) mbar_init(&S.a_empty[d][s], 2);
         }
         for (int i = 0; i < 4; ++i) {
             for (int s = 0; s < 4; ++s) {
@@ -413,7 +305,6 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
     unsigned long long* s_keys = reinterpret_cast<unsigned long long*>(smem + a.off_keys);
     unsigned char* s_B = smem + a.off_b;
     float2* s_fs = reinterpret_cast<float2*>(smem + a.off_fs);
-    uint4* s_stash = reinterpret_cast<uint4*>(smem + a.off_stash);  // [2][kDecStash][128] scale|bias words
     float* s_red = reinterpret_cast<float*>(smem + a.off_red);      // [2][T][128] tile-end partials
     unsigned char* s_ring = smem + a.off_ring;
     tc_before_sync();
@@ -452,7 +343,9 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
         }
         __syncthreads();
         if (tid == 0) dstamp_thread(a, 22);
-        if (a.logits) route_tokens(s_logits, s_keys, S.nan_tok, a.M, a.E, a.K, 0, nthr, 0, S.inds, S.scores, a.trace);
+        if (a.logits)
+            route_tokens(s_logits, s_keys, S.nan_tok, a.M, a.E, a.K, 0, nthr, 0, S.inds, S.scores,
+                         a.trace ? a.trace + (size_t)blockIdx.x * kTracePointsDec + 25 : nullptr);
         __syncthreads();
         if (tid == 0) dstamp_thread(a, 23);
         if (warp == 0) plan_units_warp(S.inds, P, a.E, a.K, T, S.units, S.sorted, S.qinfo, &S.nunits, &S.bad);
@@ -498,7 +391,11 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
     // groups of warpgroup d in chunk c of a phase with nG groups (0 or 4: nG % 4 == 0)
     auto wg_groups = [](int nG, int c, int d) { return min(4, max(0, min(8, nG - 8 * c) - 4 * d)); };
 
-    if (warp >= kWarpProd0) {
+    if (warp >= kWarpMma0) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kDecRegsCtl));
+    else asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kDecRegsWork));
+    if (warp >= kWarpProd0 + kDecProducers) {
+        // idle
+    } else if (warp >= kWarpProd0) {
         // ---- TMA producers: item i (phase, tile, chunk) fills stage i % S_ -------------
         // ---- (codes, then scales, then biases); producer i % 2 (S_ is even) -----------
         if (lane == 0) {
@@ -598,18 +495,10 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                         if (wg_groups(nG, c, d) == 0) continue;
                         const int slot = ua % kDecAslots;
                         const long long tw0 = a.trace ? gtime() : 0;
-                        // the four warps of the warpgroup have written the slot (acquire)
-                        {
-                            const int want = 4 * (ua / kDecAslots + 1);
-                            const volatile int* ready = &S.a_ready[d][slot];
-                            int it = 0;
-                            while (ld_acquire_shared(ready) < want) {
-                                if (++it > a.spin_limit || ((it & 255) == 0 && *abort_flag)) {
-                                    okm = false;
-                                    break;
-                                }
-                            }
-                            if (!okm) break;
+                        // the four warps of the warpgroup have written the slot
+                        if (!mbar_wait_bounded(&S.a_full[d][slot], (ua / kDecAslots) & 1, a.spin_limit, abort_flag)) {
+                            okm = false;
+                            break;
                         }
                         if (a.trace) wait_a += gtime() - tw0;
                         tc_after_sync();
@@ -643,7 +532,7 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                             }
                         }
                         if (!okm) break;
-                        mma_commit(&S.a_empty[d][slot][hh]);
+                        mma_commit(&S.a_empty[d][slot]);
                         if (a.trace) cy_issue += clock64() - cyi;
                         ++ua;
                     }
@@ -665,85 +554,81 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
     } else if (warp < kWarpEpi0) {
         // ---- dequantising warpgroup d: groups [4d, 4d + 4) of every stage ---------------
         // ---- (16-byte chunks 4d .. 4d + 3 of a 128-byte stage row); lane L = tile row --
+        // Software-pipelined: the next item's codes are read while this item's
+        // tensor-memory stores complete.
         const int d = warp >> 2, L = (warp & 3) * 32 + lane;
         const uint32_t lane_off = tmem_lane_base(warp);
         const uint32_t tA0 = tmem + d * 256;
-        int item = 0, ua = 0, uc = 0;
         bool okd = true;
         long long w_full = 0, w_a = 0;
-        for (int ph = 0; ph < 2; ++ph) {
-            const int nt = ph ? nt_dn : nt_up, nC = ph ? nC_dn : nC_up, nG = ph ? nG_dn : nG_up;
-            for (int t = 0; t < nt; ++t) {
-                for (int c = 0; c < nC; ++c, ++item) {
-                    const int s = item % S_;
+        // stream position: item number and its (phase, tile, chunk)
+        int item = 0, ph = 0, t = 0, c = 0;
+        auto settle = [&]() {
+            while (ph < 2 && t >= (ph ? nt_dn : nt_up)) {
+                ++ph;
+                t = 0;
+            }
+        };
+        settle();
+        // Reads the codes of the next item with groups for this warpgroup into
+        // `raw` (and releases the stages of the items before it, which hold
+        // nothing for it); false at the end of the stream.
+        auto fetch = [&](uint4 (&raw)[4]) -> bool {
+            while (ph < 2) {
+                const int s = item % S_;
+                const bool mine = wg_groups(ph ? nG_dn : nG_up, c, d) > 0;
+                if (mine) {
                     const long long tw0 = a.trace ? gtime() : 0;
                     if (okd) okd = mbar_wait_warp(&S.full[s], (item / S_) & 1, a.spin_limit, abort_flag);
                     if (a.trace) w_full += gtime() - tw0;
-                    const int cnt = wg_groups(nG, c, d);
-                    uint4 raw[4];
-                    uint2 sbw = make_uint2(0u, 0u);
-                    if (cnt > 0 && okd) {
-                        const unsigned char* stg = s_ring + (size_t)s * kDecStageBytes;
-                        const unsigned char* row = stg + L * 128;
+                    if (okd) {
+                        const unsigned char* row = s_ring + (size_t)s * kDecStageBytes + L * 128;
 #pragma unroll
                         for (int j = 0; j < 4; ++j)
                             raw[j] = *reinterpret_cast<const uint4*>(row + (((4 * d + j) ^ (L & 7)) << 4));
-                        // the four groups' scales and biases (gs 128: two scales, one word)
-                        const int so = (GS == 64) ? 8 * d : 8 * (c & 1) + 4 * d;
-                        if (GS == 64) {
-                            sbw.x = *reinterpret_cast<const uint32_t*>(stg + kDecCodeBytes + L * 16 + so);
-                            sbw.y = *reinterpret_cast<const uint32_t*>(stg + kDecCodeBytes + L * 16 + so + 4);
-                        } else {
-                            sbw.x = *reinterpret_cast<const uint32_t*>(stg + kDecCodeBytes + L * 16 + so);
-                        }
-                        uint2 bbw = make_uint2(0u, 0u);
-                        bbw.x = *reinterpret_cast<const uint32_t*>(stg + kDecCodeBytes + kDecSbBytes + L * 16 + so);
-                        if (GS == 64)
-                            bbw.y = *reinterpret_cast<const uint32_t*>(stg + kDecCodeBytes + kDecSbBytes + L * 16 + so + 4);
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&S.empty[s]);  // the stage is in registers now
-                        // scale/bias words for the epilogue warpgroup
-                        const int sl = uc % kDecStash;
-                        if (uc >= kDecStash)
-                            okd = mbar_wait_warp(&S.sb_empty[d][sl], ((uc - kDecStash) / kDecStash) & 1, a.spin_limit,
-                                                 abort_flag);
-                        if (okd) {
-                            s_stash[((size_t)d * kDecStash + sl) * 128 + L] = make_uint4(sbw.x, sbw.y, bbw.x, bbw.y);
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&S.sb_full[d][sl]);
-                        }
-                        ++uc;
-                        // the A operand: four class words per code word, 16 columns per group
-                        const int slot = ua % kDecAslots;
-                        const long long tw1 = a.trace ? gtime() : 0;
-                        for (int h = 0; h < 2; ++h)
-                            if (okd && ua >= kDecAslots)
-                                okd = mbar_wait_warp(&S.a_empty[d][slot][h], ((ua - kDecAslots) / kDecAslots) & 1,
-                                                     a.spin_limit, abort_flag);
-                        if (a.trace) w_a += gtime() - tw1;
-                        if (okd) {
-                            tc_after_sync();
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                const uint32_t wv[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
-                                uint32_t m[16];
-#pragma unroll
-                                for (int p = 0; p < 4; ++p)
-#pragma unroll
-                                    for (int i = 0; i < 4; ++i) m[4 * p + i] = wv[i] & (0x03030303u << (2 * p));
-                                tmem_st16(tA0 + slot * 64 + j * 16 + lane_off, m);
-                            }
-                            tmem_st_wait();
-                            tc_before_sync();
-                            __syncwarp();
-                            if (lane == 0) red_release_add_shared(&S.a_ready[d][slot], 1);
-                        }
-                        ++ua;
-                    } else {
-                        __syncwarp();
-                        if (lane == 0 && okd) mbar_arrive(&S.empty[s]);
                     }
                 }
+                __syncwarp();
+                if (lane == 0 && okd) mbar_arrive(&S.empty[s]);  // in registers now (or nothing to read)
+                ++item;
+                if (++c == (ph ? nC_dn : nC_up)) {
+                    c = 0;
+                    ++t;
+                    settle();
+                }
+                if (mine) return true;
+            }
+            return false;
+        };
+        uint4 raw[4];
+        bool have = fetch(raw);
+        for (int ua = 0; have; ++ua) {
+            // the A operand: four class words per code word, 16 columns per group
+            const int slot = ua % kDecAslots;
+            const long long tw1 = a.trace ? gtime() : 0;
+            if (okd && ua >= kDecAslots)
+                okd = mbar_wait_warp(&S.a_empty[d][slot], ((ua - kDecAslots) / kDecAslots) & 1, a.spin_limit,
+                                     abort_flag);
+            if (a.trace) w_a += gtime() - tw1;
+            if (okd) {
+                tc_after_sync();
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t wv[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+                    uint32_t m[16];
+#pragma unroll
+                    for (int p = 0; p < 4; ++p)
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) m[4 * p + i] = wv[i] & (0x03030303u << (2 * p));
+                    tmem_st16(tA0 + slot * 64 + j * 16 + lane_off, m);
+                }
+            }
+            have = fetch(raw);
+            if (okd) {
+                tmem_st_wait();
+                tc_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.a_full[d][slot]);
             }
         }
         if (!okd) *abort_flag = 1;
@@ -757,7 +642,7 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
         const int te = tid - kTidEpi0;  // 0 .. 255
         const uint32_t lane_off = tmem_lane_base(warp);
         const uint32_t tD0 = tmem + d * 256 + 128;
-        int ude[2] = {0, 0}, uc = 0;
+        int ude[2] = {0, 0}, item = 0;
         bool oke = true;
         long long w_d = 0, cy_epi = 0;
         const bool prof = a.trace != nullptr && te == 0;
@@ -822,11 +707,30 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                 float acc[T];
 #pragma unroll
                 for (int v = 0; v < T; ++v) acc[v] = 0.f;
-                for (int c = 0; c < nC; ++c) {
-                    if (wg_groups(nG, c, d) == 0) continue;
-                    const int sl = uc % kDecStash;
-                    if (oke) oke = mbar_wait_warp(&S.sb_full[d][sl], (uc / kDecStash) & 1, a.spin_limit, abort_flag);
-                    const uint4 sbw = oke ? s_stash[((size_t)d * kDecStash + sl) * 128 + L] : make_uint4(0u, 0u, 0u, 0u);
+                for (int c = 0; c < nC; ++c, ++item) {
+                    // this warpgroup's scales and biases of the item, from its stage
+                    const int s = item % S_;
+                    if (wg_groups(nG, c, d) == 0) {
+                        __syncwarp();
+                        if (lane == 0 && oke) mbar_arrive(&S.empty[s]);
+                        continue;
+                    }
+                    uint4 sbw = make_uint4(0u, 0u, 0u, 0u);
+                    if (oke) oke = mbar_wait_warp(&S.full[s], (item / S_) & 1, a.spin_limit, abort_flag);
+                    if (oke) {
+                        const unsigned char* sbrow = s_ring + (size_t)s * kDecStageBytes + kDecCodeBytes + L * 16;
+                        if (GS == 64) {
+                            const uint2 sw = *reinterpret_cast<const uint2*>(sbrow + 8 * d);
+                            const uint2 bw = *reinterpret_cast<const uint2*>(sbrow + kDecSbBytes + 8 * d);
+                            sbw = make_uint4(sw.x, sw.y, bw.x, bw.y);
+                        } else {  // gs 128: two scales (one word) of the chunk's half of the box
+                            const int so = 8 * (c & 1) + 4 * d;
+                            sbw.x = *reinterpret_cast<const uint32_t*>(sbrow + so);
+                            sbw.z = *reinterpret_cast<const uint32_t*>(sbrow + kDecSbBytes + so);
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0 && oke) mbar_arrive(&S.empty[s]);
 #pragma unroll
                     for (int hh = 0; hh < 2; ++hh) {
                         const int iw = 2 * d + hh;
@@ -877,9 +781,6 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                             if (prof) cy_epi += clock64() - cy0;
                         }
                     }
-                    __syncwarp();
-                    if (lane == 0 && oke) mbar_arrive(&S.sb_empty[d][sl]);
-                    ++uc;
                 }
                 // ---- tile end: warpgroup partials -> (e0 + e1) -----------------------
 #pragma unroll

@@ -18,16 +18,26 @@ constexpr int kCtrlStatus = 1, kCtrlError = 2, kCtrlArrive = 3, kCtrlGen = 4;
 //   0-7   dequantise: warpgroup d (warps 4d..4d+3) turns the 16-code words of
 //         groups [4d, 4d+4) of every stage into the MMA's A operand in TMEM;
 //   8-15  epilogue: warpgroup d (warps 8+4d..) reads warpgroup d's
-//         accumulators (tcgen05.ld), applies scales and biases, writes outputs;
+//         accumulators (tcgen05.ld), applies the scales and biases (read from
+//         the stage, which both roles release), writes outputs;
 //   16-19 MMA issue (lane 0): warp 16+2d+h issues the MMAs of groups 2h, 2h+1
 //         of warpgroup d's four (a thread issues one MMA per ~60 cycles, and
 //         the issue rate grows with the number of issuing warps);
-//   20-21 TMA producers (lane 0), alternate stages.
+//   20-21 TMA producers (lane 0), alternate stages; 22-23 idle.
 constexpr int kDecDeqWarps = 8;
 constexpr int kDecEpiWarps = 8;
 constexpr int kDecMmaWarps = 4;
 constexpr int kDecProducers = 2;
-constexpr int kDecThreadsAll = 32 * (kDecDeqWarps + kDecEpiWarps + kDecMmaWarps + kDecProducers);
+constexpr int kDecIdleWarps = 2;  // complete the producers' warpgroup (registers move per warpgroup)
+constexpr int kDecThreadsAll = 32 * (kDecDeqWarps + kDecEpiWarps + kDecMmaWarps + kDecProducers + kDecIdleWarps);
+// Registers per thread after the role split (setmaxnreg): the dequantising and
+// epilogue warpgroups take what the MMA / producer warpgroups give up; the sum
+// stays within the launch's 80 x kDecThreadsAll.
+constexpr int kDecRegsWork = 96, kDecRegsCtl = 40;
+static_assert(32 * (kDecDeqWarps + kDecEpiWarps) * kDecRegsWork +
+                      32 * (kDecMmaWarps + kDecProducers + kDecIdleWarps) * kDecRegsCtl <=
+                  80 * kDecThreadsAll,
+              "register split exceeds the launch's registers");
 constexpr int kDecEpiThreads = 32 * kDecEpiWarps;
 constexpr int kDecRouteThreads = 32 * (kDecMmaWarps + kDecProducers);  // route while the others encode x
 constexpr int kDecCodeBytes = 128 * 128;   // a stage's codes: 128 rows x one 128-byte K chunk (8 groups)
@@ -38,7 +48,6 @@ constexpr int kDecMaxTiles = 48;           // tiles per phase per CTA (host-chec
 constexpr int kDecMaxPairs = 64;           // M * K
 constexpr int kDecMaxLastBlocks = 64;      // (unit, 64-row block) segments per CTA in the combine
 constexpr int kDecAslots = 2;              // A slots per warpgroup (64 TMEM columns each)
-constexpr int kDecStash = 4;               // scale/bias stash slots per warpgroup (chunks)
 constexpr int kDecTmemCols = 512;
 constexpr int kTracePointsDec = 32;
 // TMA maps: 2D over [rows, row bytes] with box heights 64, 16, 8 (index 0..2),
@@ -72,7 +81,7 @@ struct DecodeArgs {
     int spin_limit;          // polls of a bounded wait before it gives up
     float clamp;
     // dynamic shared-memory carve-up (byte offsets from the 1024-aligned base)
-    int off_ring, off_b, off_fs, off_stash, off_red, off_logits, off_keys;
+    int off_ring, off_b, off_fs, off_red, off_logits, off_keys;
     int b_bytes;             // bytes of the B region
 };
 

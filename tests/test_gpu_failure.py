@@ -53,8 +53,9 @@ def _rel(y, ref):
     return float((np.sqrt(((g - r) ** 2).sum(axis=1)) / np.sqrt((r ** 2).sum(axis=1))).max())
 
 
-def test_wait_timeout_is_reported_and_the_workspace_stays_usable():
-    L = _layer()
+@pytest.mark.parametrize("M", [1, 2])  # the single-token engine and the tcgen05 kernel
+def test_wait_timeout_is_reported_and_the_workspace_stays_usable(M):
+    L = _layer(M=M)
     ws = moe.new_workspace(L["M"], L["K"], L["H"], L["I"])
     try:
         moe.set_spin_limit(-1)
