@@ -458,7 +458,9 @@ def run_gpu(args, cfg) -> None:
     if avg[moe.KERNEL_LAYER]:
         # the whole layer is one kernel, the only launch of the layer in the
         # timed graph: its duration there is ms_per_step / L
-        dom_kernel = "moe_decode_kernel (route + up||gate/SwiGLU + down + combine, tcgen05)"
+        dom_kernel = ("moe_layer_kernel (route + up||gate/SwiGLU + down + combine, warp-level u8xs8 mma)"
+                      if M == 1 and os.environ.get("MOMIJ_DECODE_M1") != "tc" else
+                      "moe_decode_kernel (route + up||gate/SwiGLU + down + combine, tcgen05)")
         dom_bytes = (sum(uniq) / L) * eb
         dom_ms = timed_layer_ms
         dom_source = "timed graph: ms_per_step / layers (one launch per layer)"
@@ -504,8 +506,11 @@ def run_gpu(args, cfg) -> None:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": ("bf16 tcgen05 GEMM (weights as hi+lo bf16), f32 accumulate, bf16 I/O"
-                      if cfg.get("zipf") else "tcgen05.mma kind::i8 (u8 code classes x s8 activation "
-                      "digits -> s32 in TMEM), f32 scale/bias epilogue, bf16 I/O"),
+                      if cfg.get("zipf") else
+                      "u8 code classes x s8 activation digits -> s32 (mma.sync m16n8k32), f32 scale/bias "
+                      "epilogue, bf16 I/O" if M == 1 and os.environ.get("MOMIJ_DECODE_M1") != "tc" else
+                      "tcgen05.mma kind::i8 (u8 code classes x s8 activation digits -> s32 in TMEM), f32 "
+                      "scale/bias epilogue, bf16 I/O"),
             "data": "synthetic (seeded generator, momij_b200/synth.py)",
             "config": {"workload": cfg["desc"], "H": H, "E": E, "top_k": K, "I": I, "gs": gs,
                        "M": M, "layers": L, "global_batch": M * world,

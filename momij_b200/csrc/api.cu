@@ -391,27 +391,25 @@ int run_decode_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws,
     a.clamp = c.clamp;
 
     // shared memory: ring of stages (codes + scales + biases) | B | per-group
-    // factors | tile-end partials; the logits and router
-    // keys live in the ring (the producers start only after the routing)
+    // factors | tile-end partials; the logits live in the ring (the producers
+    // start only after the routing)
     const size_t b_bytes = (size_t)std::max(nG_up, 2 * nG_dn) * dec_b_group_bytes(N);
     const size_t fs_bytes = align_up(8 * (size_t)std::max(c.M * nG_up, 2 * T * nG_dn), 16);
     const size_t red_bytes = (size_t)2 * T * 128 * 4;
     const size_t lg_bytes = align_up(4 * (size_t)(c.logits ? c.M * c.E : 0), 16);
-    const size_t key_bytes = align_up(8 * (size_t)(c.logits ? c.M * c.E : 0), 16);
     const size_t fixed = align_up(b_bytes, 1024) + fs_bytes + red_bytes + 1024;
     int optin = 0, dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     const long long room = (long long)optin - kDecStaticReserve - (long long)fixed;
     int stages = (int)std::min<long long>(kDecMaxStages, room / kDecStageBytes) & ~1;
-    if (stages < 2 || (size_t)stages * kDecStageBytes < lg_bytes + key_bytes) return kNotApplicable;
+    if (stages < 2 || (size_t)stages * kDecStageBytes < lg_bytes) return kNotApplicable;
     size_t off = 0;
     a.off_ring = (int)off; off += (size_t)stages * kDecStageBytes;
     a.off_b = (int)off; off += align_up(b_bytes, 1024);
     a.off_fs = (int)off; off += fs_bytes;
     a.off_red = (int)off; off += red_bytes;
     a.off_logits = a.off_ring;
-    a.off_keys = a.off_ring + (int)lg_bytes;
     const size_t smem = off + 1024;  // + alignment of the base to 1024 B
     a.stages = stages;
     a.b_bytes = (int)b_bytes;
@@ -509,7 +507,6 @@ int run_layer_engine(const LayerCall& c, int dtype, int gs, const Workspace& ws,
     size_t off = 0;
     a.off_logits = (int)off; off += a.logits ? 4 * (size_t)a.M * a.E : 0;
     off = align_up(off, 16);
-    a.off_keys = (int)off; off += a.logits ? 8 * (size_t)a.M * a.E : 0;
     a.off_inds = (int)off; off += 4 * (size_t)P;
     a.off_scores = (int)off; off += 4 * (size_t)P;
     a.off_sorted = (int)off; off += 4 * (size_t)P;

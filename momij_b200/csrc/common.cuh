@@ -193,7 +193,7 @@ __device__ inline bool grid_barrier_thread(unsigned* arrive, unsigned* gen, int 
     const unsigned g0 = ld_acquire_u32(gen);
     const unsigned old = atomicAdd(arrive, 1u);
     if (old == gridDim.x - 1) {
-        atomicExch(arrive, 0u);
+        *reinterpret_cast<volatile unsigned*>(arrive) = 0u;  // no other CTA touches it before the generation moves
         __threadfence();
         atomicAdd(gen, 1u);
         return true;

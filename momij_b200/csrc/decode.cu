@@ -302,7 +302,6 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
         S.stopped = 0;
     }
     float* s_logits = reinterpret_cast<float*>(smem + a.off_logits);
-    unsigned long long* s_keys = reinterpret_cast<unsigned long long*>(smem + a.off_keys);
     unsigned char* s_B = smem + a.off_b;
     float2* s_fs = reinterpret_cast<float2*>(smem + a.off_fs);
     float* s_red = reinterpret_cast<float*>(smem + a.off_red);      // [2][T][128] tile-end partials
@@ -344,7 +343,7 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
         __syncthreads();
         if (tid == 0) dstamp_thread(a, 22);
         if (a.logits)
-            route_tokens(s_logits, s_keys, S.nan_tok, a.M, a.E, a.K, 0, nthr, 0, S.inds, S.scores,
+            route_tokens(s_logits, S.nan_tok, a.M, a.E, a.K, 0, nthr, 0, S.inds, S.scores,
                          a.trace ? a.trace + (size_t)blockIdx.x * kTracePointsDec + 25 : nullptr);
         __syncthreads();
         if (tid == 0) dstamp_thread(a, 23);

@@ -81,7 +81,7 @@ struct DecodeArgs {
     int spin_limit;          // polls of a bounded wait before it gives up
     float clamp;
     // dynamic shared-memory carve-up (byte offsets from the 1024-aligned base)
-    int off_ring, off_b, off_fs, off_red, off_logits, off_keys;
+    int off_ring, off_b, off_fs, off_red, off_logits;
     int b_bytes;             // bytes of the B region
 };
 

@@ -240,7 +240,6 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
     const int P = a.M * a.K;
 
     float* s_logits = reinterpret_cast<float*>(smem + a.off_logits);
-    unsigned long long* s_keys = reinterpret_cast<unsigned long long*>(smem + a.off_keys);
     int* s_inds = reinterpret_cast<int*>(smem + a.off_inds);
     float* s_scores = reinterpret_cast<float*>(smem + a.off_scores);
     int* s_sorted = reinterpret_cast<int*>(smem + a.off_sorted);
@@ -266,15 +265,16 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
     pdl_wait();  // the previous kernel on the stream (e.g. the layer before) is complete
     pdl_launch_dependents();
     stamp(a, 1);
-    if (tid == 0) s_stopped = (a.stop && __ldcg(a.stop) != 0) ? 1 : 0;
 
     // ---- 1. token encoding (it does not depend on the routing), routing ----
     const int nlog = a.logits ? a.M * a.E : 0;
     const float lg0 = tid < nlog ? __ldcg(a.logits + tid) : 0.f;  // in flight during the encoding
+    const int stop0 = (tid == 0 && a.stop) ? __ldcg(a.stop) : 0;
     if (tid < a.M) up_tb.vecs[tid] = tid;
     if (tid < 8) s_nan[tid] = 0;
     __syncthreads();
     digitize<DT>(a.x, up_tb.vecs, a.M, a.H, s_dig, s_fs, kConsumerThreads);
+    if (tid == 0) s_stopped = stop0 != 0;
     if (tid < nlog) {
         s_logits[tid] = lg0;
         if (isnan(lg0)) s_nan[tid / a.E] = 1;
@@ -292,12 +292,15 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
     }
     __syncthreads();
     stamp(a, 2);
-    if (a.logits) {
-        route_tokens(s_logits, s_keys, s_nan, a.M, a.E, a.K, 0, kLayerThreads, 0, s_inds, s_scores);
-        __syncthreads();
-    }
-    if (tid < 32)
+    // selection (ends with a block barrier), then the plan (warp 0) beside the scores (warps 1..M)
+    if (a.logits) route_tokens(s_logits, s_nan, a.M, a.E, a.K, 0, kLayerThreads, 0, s_inds, s_scores,
+                               nullptr, false);
+    if (tid < 32) {
         plan_warp(s_inds, P, a.E, TMAX, s_units, s_sorted, reinterpret_cast<int4*>(s_pflag), &s_nunits, &s_bad);
+    } else if (a.logits && (tid >> 5) <= a.M) {
+        const int m = (tid >> 5) - 1;
+        route_scores_warp(s_logits + m * a.E, a.E, a.K, s_inds + m * a.K, s_scores + m * a.K);
+    }
     __syncthreads();
     const bool ok = s_bad == 0;
     const bool stopped = s_stopped != 0;

@@ -44,7 +44,7 @@ struct LayerArgs {
     int max_tiles, max_units, max_vec;  // capacities of the shared-memory tables
     long long* trace;  // optional: kTracePointsDec %globaltimer stamps per CTA (thread 0)
     // dynamic shared-memory carve-up (byte offsets)
-    int off_logits, off_keys, off_inds, off_scores, off_sorted, off_pflag, off_units;
+    int off_logits, off_inds, off_scores, off_sorted, off_pflag, off_units;
     int off_tiles_up, off_lunits_up, off_upair_up, off_uslot_up, off_seg_up, off_xvecs;
     int off_tiles_dn, off_lunits_dn, off_upair_dn, off_uslot_dn, off_seg_dn, off_vecs_dn;
     int off_fs, off_dig, off_red, off_sb, off_stage;

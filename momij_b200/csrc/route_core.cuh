@@ -116,34 +116,18 @@ __device__ __forceinline__ void route_scores_warp(const float* __restrict__ lg, 
     if (lane < K) scores[lane] = gate / s;
 }
 
-// Order of two candidates of the reference's reduction tree (see
-// route_topk_tree): a larger value wins; equal values (signed zeros compare
-// equal) go to the expert whose bit-reversed index (over the tree's width) is
-// smaller.  `rb` is the bit count of the width (8 for E <= 256).
-__device__ __forceinline__ uint32_t route_value_key(float v) {
-    uint32_t u = __float_as_uint(v);
-    if ((u & 0x7fffffffu) == 0) u = 0;  // -0 == +0
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ uint32_t rev_index(int e, int rb) { return __brev((uint32_t)e) >> (32 - rb); }
 
 // Router of the M tokens by the `nthr` threads from thread `t0` (a named
-// barrier `bar` over them): 64-bit keys (value order, then the reference's
-// tree order on ties: the smaller bit-reversed index) in shared memory, then
-// candidate (m, e) lands at position #{e' : key(e') > key(e)} when that is
-// below K.  Tokens with a NaN logit take the reference's tree step by step
-// (route_topk_tree).  Scores: route_scores_warp.
-__device__ inline void route_tokens(const float* s_logits, unsigned long long* s_keys, const int* s_nan, int M,
-                             int E, int K, int t0, int nthr, int bar, int* s_inds, float* s_scores,
-                             long long* stamp_ranks = nullptr) {
+// barrier `bar` over them): candidate (m, e) lands at position
+// #{e' : l(e') > l(e), or l(e') == l(e) and rev(e') < rev(e)} when that is
+// below K -- value order, then the reference's tree order on ties (the
+// smaller bit-reversed index); the float compare makes signed zeros equal.  Tokens with a NaN logit take the reference's tree step by step
+// (route_topk_tree).  Scores (route_scores_warp) unless `with_scores` is
+// false: the caller then computes them, e.g. beside other work.
+__device__ inline void route_tokens(const float* s_logits, const int* s_nan, int M,
+                                    int E, int K, int t0, int nthr, int bar, int* s_inds, float* s_scores,
+                                    long long* stamp_ranks = nullptr, bool with_scores = true) {
     const int t = threadIdx.x - t0;
-    const int rb = 31 - __clz(route_tree_width(E));
-    for (int c = t; c < M * E; c += nthr) {
-        const int e = c % E;
-        s_keys[c] = ((unsigned long long)route_value_key(s_logits[c]) << 32) |
-                    (unsigned long long)(0xffffffffu - rev_index(e, rb));
-    }
-    bar_sync(bar, nthr);
     constexpr int kParts = 8;  // threads per candidate
     for (int base = 0; base < M * E * kParts; base += nthr) {
         const int it = base + t;
@@ -152,10 +136,15 @@ __device__ inline void route_tokens(const float* s_logits, unsigned long long* s
         const bool valid = c < M * E;
         const int m = valid ? c / E : 0;
         if (valid && !s_nan[m]) {
-            const unsigned long long kc = s_keys[c];
-            const unsigned long long* kr = s_keys + m * E;
+            const float* lr = s_logits + m * E;
+            const int e = c - m * E;
+            const float lc = lr[e];
+            const unsigned rc = __brev((unsigned)e);  // bit-reversed order of any power-of-two width
 #pragma unroll 8
-            for (int j = sub; j < E; j += kParts) r += kr[j] > kc;
+            for (int j = sub; j < E; j += kParts) {
+                const float lj = lr[j];
+                r += (lj > lc) | ((lj == lc) & (__brev((unsigned)j) < rc));
+            }
         }
 #pragma unroll
         for (int o = 1; o < kParts; o <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
@@ -173,7 +162,8 @@ __device__ inline void route_tokens(const float* s_logits, unsigned long long* s
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tt));
         *stamp_ranks = (long long)tt;
     }
-    for (int m = w; m < M; m += nw) route_scores_warp(s_logits + m * E, E, K, s_inds + m * K, s_scores + m * K);
+    if (with_scores)
+        for (int m = w; m < M; m += nw) route_scores_warp(s_logits + m * E, E, K, s_inds + m * K, s_scores + m * K);
 }
 
 // Both steps for one token.
