@@ -146,6 +146,8 @@ struct Workspace {
     float* scores;
     unsigned* block_ctr;
     int32_t* grp;  // grouped path: offsets [1025], pair [P], weight [P] (float), block list (16-B aligned)
+    int32_t* fix;  // grouped path: act outputs to recompute exactly (count, pad, then int2 entries)
+    int fix_cap;
     size_t bytes;
 };
 
@@ -174,6 +176,11 @@ Workspace carve(void* ws, int M, int Ktop, int H, int I) {
     off += align_up((size_t)((H + 63) / 64) * 4, 256);
     w.grp = reinterpret_cast<int32_t*>(p + off);
     off += align_up(4 * (kGrpOffsets + 2 * P + 4 + block_list_ints((int)P, kGrpMaxExperts)), 256);
+    // one entry per 8 (pair, row) outputs of up||gate: the fraction near a
+    // rounding midpoint is ~1 % (bf16) to ~3 % (fp16)
+    w.fix = reinterpret_cast<int32_t*>(p + off);
+    w.fix_cap = (int)std::min<size_t>((P * (size_t)I + 7) / 8, (size_t)1 << 27);
+    off += align_up(16 + 16 * (size_t)w.fix_cap, 256);
     w.bytes = off;
     return w;
 }
@@ -820,6 +827,12 @@ bool grouped_enabled(int M, int Ktop, int E) {
 }
 
 using GroupedFn = void (*)(const GroupedArgs);
+using FixupFn = void (*)(const FixupArgs);
+FixupFn pick_fixup(int dtype, int gs) {
+    if (dtype == MOMIJ_DTYPE_BF16)
+        return gs == 64 ? act_fixup_kernel<MOMIJ_DTYPE_BF16, 64> : act_fixup_kernel<MOMIJ_DTYPE_BF16, 128>;
+    return gs == 64 ? act_fixup_kernel<MOMIJ_DTYPE_F16, 64> : act_fixup_kernel<MOMIJ_DTYPE_F16, 128>;
+}
 template <int DT, int GS>
 GroupedFn pick_grouped_dt(int mode) {
     return mode == kModeUpSwiglu ? grouped_gemm_kernel<DT, GS, kModeUpSwiglu> : grouped_gemm_kernel<DT, GS, kModeRows>;
@@ -844,7 +857,9 @@ int run_grouped(const void* x, const uint32_t* w_ug, const void* s_ug, const voi
     float* weight = reinterpret_cast<float*>(pair + P);
     // the block list is read as int4 entries: 16-byte aligned (the region has 4 ints of slack)
     int32_t* blocks = reinterpret_cast<int32_t*>(align_up(reinterpret_cast<uintptr_t>(weight + P), 16));
-    if (cudaMemsetAsync(hdr + 1, 0, sizeof(int32_t), st) != cudaSuccess) return MOMIJ_ERR_CUDA;
+    if (cudaMemsetAsync(hdr + 1, 0, sizeof(int32_t), st) != cudaSuccess ||
+        cudaMemsetAsync(ws.fix, 0, sizeof(int32_t), st) != cudaSuccess)
+        return MOMIJ_ERR_CUDA;
     const int G = current_device_sm_count();
     if (G <= 0) return MOMIJ_ERR_CUDA;
     int slot = prof_begin(MOMIJ_KERNEL_PLAN, st);
@@ -884,11 +899,31 @@ int run_grouped(const void* x, const uint32_t* w_ug, const void* s_ug, const voi
         a.clamp = clamp;
         a.E = E;
         a.P = P;
+        a.fix = mode == kModeUpSwiglu ? ws.fix : nullptr;
+        a.fix_cap = ws.fix_cap;
+        a.fix_ulps = fix_ulps_for(H);
         GroupedFn fn = pick_grouped(dtype, gs, mode);
         if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return MOMIJ_ERR_CUDA;
         slot = prof_begin(mode == kModeUpSwiglu ? MOMIJ_KERNEL_UP : MOMIJ_KERNEL_ROWS, st);
         rc = cuda_status(launch(fn, dim3(G), dim3(kGroupedThreads), smem, st, a));
+        if (!rc && mode == kModeUpSwiglu) {  // the listed act values, exactly
+            FixupArgs f{};
+            f.x = static_cast<const uint16_t*>(x);
+            f.w = w_ug;
+            f.s = static_cast<const uint16_t*>(s_ug);
+            f.b = static_cast<const uint16_t*>(b_ug);
+            f.inds = inds;
+            f.fix = ws.fix;
+            f.status = hdr;
+            f.act = ws.act;
+            f.Kd = H;
+            f.I = I;
+            f.Ktop = Ktop;
+            f.fix_cap = ws.fix_cap;
+            f.clamp = clamp;
+            rc = cuda_status(launch(pick_fixup(dtype, gs), dim3(4 * G), dim3(256), 0, st, f));
+        }
         prof_end(slot, st);
         if (rc) return rc;
     }

@@ -101,6 +101,37 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 }
 // Column of element c in class order: within each block of 16 elements,
 // element 4j + p moves to 4p + j (the order the dequantised weight tiles use).
+// Whether v lies within `ulps` fp32 ulps of a rounding midpoint of the
+// 16-bit type (normal range of the type).
+template <int DT>
+__device__ __forceinline__ bool near_half_midpoint(float v, int ulps) {
+    const uint32_t u = __float_as_uint(v);
+    if (DT == MOMIJ_DTYPE_BF16) return abs((int)(u & 0xffffu) - 0x8000) < ulps;
+    return abs((int)(u & 0x1fffu) - 0x1000) < ulps;
+}
+
+// s + e = a + b exactly (Knuth's two-sum), e accumulated.
+__device__ __forceinline__ void two_sum_acc(float& s, float& e, float b) {
+    const float t = s + b;
+    const float bv = t - s;
+    e += (s - (t - bv)) + (b - bv);
+    s = t;
+}
+
+// float64 -> 16-bit value, rounded once (ties to even), as the oracle does.
+template <int DT>
+__device__ __forceinline__ uint16_t half_from_f64(double d) {
+    constexpr int kMant = (DT == MOMIJ_DTYPE_BF16) ? 7 : 10;
+    constexpr int kEmin = (DT == MOMIJ_DTYPE_BF16) ? -126 : -14;
+    if (isnan(d)) return Half<DT>::from_f(__int_as_float(0x7fc00000));
+    const double m = fabs(d);
+    if (m == 0.0) return Half<DT>::from_f((float)d);
+    const int e = max(ilogb(m), kEmin);
+    const double q = ldexp(1.0, e - kMant);
+    const double v = copysign(rint(m / q) * q, d);  // representable in the 16-bit type (or overflowing to inf)
+    return Half<DT>::from_f((float)v);              // exact conversion
+}
+
 __device__ __forceinline__ int class_order16(int c) {
     return (c & ~15) | ((c & 3) << 2) | ((c >> 2) & 3);
 }
@@ -517,8 +548,20 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
                             const int n = c0 + cc + j;
                             if (n < cnt) {  // act columns in class order for the down GEMM
                                 const int p = min(max(__ldg(a.pairs + start + n), 0), a.P - 1);
+                                const float uf = __uint_as_float(v[j]), gf = sG[n * 64 + r];
+                                const int which = a.fix ? (near_half_midpoint<DT>(uf, a.fix_ulps) ? 1 : 0) |
+                                                              (near_half_midpoint<DT>(gf, a.fix_ulps) ? 2 : 0)
+                                                        : 0;
+                                if (which) {
+                                    const int q = atomicAdd(a.fix, 1);
+                                    if (q < a.fix_cap) {
+                                        reinterpret_cast<int4*>(a.fix + 4)[q] = make_int4(
+                                            p, rb * 64 + r, which, __float_as_int(which == 1 ? gf : uf));
+                                        continue;  // act_fixup_kernel writes it
+                                    }
+                                }
                                 a.out[(size_t)p * a.Ru + class_order16(rb * 64 + r)] =
-                                    swiglu_staged<DT>(__uint_as_float(v[j]), sG[n * 64 + r], a.clamp);
+                                    swiglu_staged<DT>(uf, gf, a.clamp);
                             }
                         }
                     }
@@ -555,9 +598,60 @@ __global__ void __launch_bounds__(kGroupedThreads, 1) grouped_gemm_kernel(const 
     pdl_launch_dependents();
 }
 
+template <int DT, int GS>
+__global__ void __launch_bounds__(256) act_fixup_kernel(const FixupArgs a) {
+    pdl_wait();  // the up||gate GEMM (the list, act) is complete
+    pdl_launch_dependents();
+    if (__ldcg(a.status + 1) != 0 || __ldcg(a.status + 2) != 0) return;  // routing failed or a wait gave up
+    const int n = min(__ldcg(a.fix), a.fix_cap);
+    const int lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
+    constexpr int kWpg = GS / 16;  // code words per scale group
+    const int ng = a.Kd / GS;
+    for (int it = blockIdx.x * wpb + (threadIdx.x >> 5); it < n; it += gridDim.x * wpb) {
+        const int4 ent = __ldcg(reinterpret_cast<const int4*>(a.fix + 4) + it);
+        const int p = ent.x, i = ent.y, which = ent.z, e = a.inds[p];
+        const uint16_t* xr = a.x + (size_t)(p / a.Ktop) * a.Kd;
+        float sums[2] = {__int_as_float(ent.w), __int_as_float(ent.w)};  // [up, gate]
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+            if (!((which >> h) & 1)) continue;
+            const size_t row = (size_t)e * 2 * a.I + (size_t)h * a.I + i;
+            const uint32_t* wr = a.w + row * (a.Kd / 16);
+            const uint16_t* sr = a.s + row * ng;
+            const uint16_t* br = a.b + row * ng;
+            double acc = 0.0;
+            for (int g = lane; g < ng; g += 32) {  // lane: whole scale groups
+                float sq = 0.f, eq = 0.f, sx = 0.f, ex = 0.f;
+#pragma unroll
+                for (int wq = 0; wq < kWpg; ++wq) {
+                    const uint32_t c = __ldg(wr + g * kWpg + wq);
+                    const uint4* xv = reinterpret_cast<const uint4*>(xr + (size_t)g * GS + wq * 16);
+                    const uint4 x0 = __ldg(xv), x1 = __ldg(xv + 1);
+                    const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float xf = Half<DT>::to_f((uint16_t)(xw[j >> 1] >> (16 * (j & 1))));
+                        const uint32_t q = (c >> (2 * j)) & 3u;
+                        const float qx = ((q & 1u) ? xf : 0.f) + ((q & 2u) ? xf + xf : 0.f);  // exact
+                        two_sum_acc(sq, eq, qx);
+                        two_sum_acc(sx, ex, xf);
+                    }
+                }
+                const double sc = Half<DT>::to_f(__ldg(sr + g)), bi = Half<DT>::to_f(__ldg(br + g));
+                acc = fma(sc, (double)sq + (double)eq, fma(bi, (double)sx + (double)ex, acc));
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            sums[h] = Half<DT>::to_f(half_from_f64<DT>(acc));
+        }
+        if (lane == 0) a.act[(size_t)p * a.I + class_order16(i)] = swiglu_staged<DT>(sums[0], sums[1], a.clamp);
+    }
+}
+
 #define MOMIJ_GROUPED_INST(DT, GS)                                               \
     template __global__ void grouped_gemm_kernel<DT, GS, kModeUpSwiglu>(const GroupedArgs); \
-    template __global__ void grouped_gemm_kernel<DT, GS, kModeRows>(const GroupedArgs);
+    template __global__ void grouped_gemm_kernel<DT, GS, kModeRows>(const GroupedArgs); \
+    template __global__ void act_fixup_kernel<DT, GS>(const FixupArgs);
 MOMIJ_GROUPED_INST(MOMIJ_DTYPE_BF16, 64)
 MOMIJ_GROUPED_INST(MOMIJ_DTYPE_BF16, 128)
 MOMIJ_GROUPED_INST(MOMIJ_DTYPE_F16, 64)

@@ -41,7 +41,44 @@ struct GroupedArgs {
     int Kd, N, Ru, Ktop;     // Ru: up||gate mode: first gate row (= I)
     int E, P;                // experts, pairs (bounds of the block list entries)
     float clamp;
+    // up||gate mode: outputs whose up or gate sum lies within fix_ulps fp32
+    // ulps of a rounding midpoint of the 16-bit type are listed here for the
+    // exact recomputation (act_fixup_kernel) instead of written: fix[0] =
+    // count, then int4 entries (pair, row, which sums: bit 0 up, bit 1 gate,
+    // the other sum's fp32 bits); entries past fix_cap are written as computed
+    int32_t* fix;
+    int fix_cap;
+    int fix_ulps;
 };
+
+// Distance (in fp32 ulps of the value) below which an up or gate sum of the
+// tensor-core GEMM is recomputed exactly.  The GEMM's fp32 accumulation is off
+// by ~10 ulps (median; ~260 at the 99th percentile, the tail being sums with
+// cancellation, whose small `act` values barely move a row) at K = 1024, and
+// about twice that at K = 4096; a sum that close to a midpoint can round to
+// the other 16-bit neighbour, and one moved `act` value shifts a whole down row.
+__host__ __device__ constexpr int fix_ulps_for(int Kd) { return Kd >= 2048 ? 128 : 64; }
+
+struct FixupArgs {
+    const uint16_t* x;       // [M, Kd] token rows (natural order)
+    const uint32_t* w;       // up||gate codes [E, 2I, Kd/16]
+    const uint16_t* s;       // [E, 2I, Kd/gs]
+    const uint16_t* b;
+    const int32_t* inds;     // [P] expert of each (token, slot) pair
+    const int32_t* fix;      // list written by the up||gate GEMM
+    const int32_t* status;   // work-plan header ([1] routing status, [2] error word)
+    uint16_t* act;           // [P, I], columns in class order
+    int Kd, I, Ktop, fix_cap;
+    float clamp;
+};
+
+// The listed (pair, row) outputs of the up||gate projection: the flagged
+// sums recomputed exactly (per scale group, the code-weighted and the plain
+// sums of the activations by error-free fp32 two-sum, combined with the
+// group's scale and bias in float64), rounded once to the activation dtype
+// like the oracle, and written through the staged clamped SwiGLU.
+template <int DT, int GS>
+__global__ void act_fixup_kernel(const FixupArgs a);
 
 // y = x with each row's 16-element blocks in class order (element 4j + p of
 // a block at 4p + j), the K order of the dequantised weight tiles; `blocks`

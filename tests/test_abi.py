@@ -35,11 +35,13 @@ def test_workspace_size_grows_with_pairs():
     # plan (header + 5 ints per pair) + act + down + inds + scores + one
     # completion counter per 64 output rows + the grouped path's tables
     # (offsets for up to 1024 experts, pair ids, weights, status words, block
-    # list of up to P/128 + 1025 blocks), 256-B aligned pieces
-    P = 8
+    # list of up to P/128 + 1025 blocks) + its exact-recomputation list (a
+    # 16-B count, 16-B entries for one in 8 up||gate outputs), 256-B aligned
+    P, I = 8, 1536
     up = lambda n: -(-n // 256) * 256
     grp = 4 * (1025 + 2 * P + 4 + 4 + 4 * (P // 128 + 1024 + 1))
-    expect = (up(4 * (4 + 5 * P)) + P * 1536 * 2 + P * 4096 * 2 + 256 + 256 + 256 + up(grp))
+    fix = 16 + 16 * -(-P * I // 8)
+    expect = (up(4 * (4 + 5 * P)) + P * I * 2 + P * 4096 * 2 + 256 + 256 + 256 + up(grp) + up(fix))
     assert a == expect
     assert moe.workspace_size(-1, 8, 16, 16) == 0
 
