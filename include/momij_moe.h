@@ -198,6 +198,54 @@ int momij_moe_forward(const float* logits, const void* x, const uint32_t* w_ug, 
                       int E, int Ktop, int gs, float clamp, int dtype, void* workspace,
                       size_t workspace_bytes, momij_stream_t stream);
 
+/* Router logits [M, E] = x [M, H] W_gate [E, H]^T, fp32 accumulation (the
+ * 16-bit x and W are widened; x_dtype and w_dtype are MOMIJ_DTYPE_*).
+ * H % 256 == 0; rows 16-byte aligned.
+ * Replaces: maple_batched_gemv / maple_gate_gemv (SeedlessMetal.swift:
+ * 2542-2595) as encoded by SeedlessMetal.encodeGate (:1143-1202), and the
+ * logits matmul of MapleMoE.route (MapleMoE.swift:52). */
+int momij_moe_router_logits(const void* x, const void* w_gate, float* logits, int M, int H, int E,
+                            int x_dtype, int w_dtype, momij_stream_t stream);
+
+/* Fused router in one launch: the gate GEMV, then per token softmax
+ * p_e = exp(l_e - max) / (sum + 1e-20), top-K over p, scores
+ * p_k / (sum_k p_k + 1e-20); ties go as in the reference's scan (a lower
+ * simdgroup, then the lane with the smaller bit-reversed index, then the lower
+ * expert keeps a tie).  counter: one device uint32, zero before the first call
+ * (each call leaves it zero; one counter per concurrently running call).
+ * logits [M, E] is scratch (left holding the logits).  M <= 64, K <= 32,
+ * E % 8 == 0, H % 256 == 0.
+ * Replaces: MapleFused.fusedRouter (MapleFused.swift:79-255), which the
+ * reference uses for one token and K = 8 (MapleMoE.swift:43-47); every token of
+ * a batch is routed alike here. */
+int momij_moe_fused_router(const void* x, const void* w_gate, uint32_t* counter, float* logits,
+                           int32_t* inds, float* scores, int M, int H, int E, int K, int x_dtype,
+                           int w_dtype, momij_stream_t stream);
+
+/* RMSNorm: out[m] = round((x[m] * inv) * w), inv = 1 / sqrt(sum x^2 / H + eps),
+ * fp32 arithmetic.
+ * Replaces: maple_rms_norm (SeedlessMetal.swift:2496-2527) as encoded by
+ * SeedlessMetal.encodeRms (:1071-1086). */
+int momij_rms_norm(const void* x, const void* w, void* out, int M, int H, float eps, int dtype,
+                   momij_stream_t stream);
+
+/* Workspace bytes of momij_moe_block: momij_moe_workspace_size plus the
+ * normalised activations [M, H] and the logits [M, E]; zero-filled once
+ * before its first use, like the momij_moe_forward workspace. */
+size_t momij_moe_block_workspace_size(int M, int Ktop, int H, int I, int E);
+
+/* One MoE block from the residual stream h [M, H], updated in place:
+ * xn = rmsnorm(h, norm_w, eps); logits = xn W_gate^T; top-K routing
+ * (momij_moe_route); h += experts(xn) with the fused score-residual rounding
+ * (momij_moe_forward with resid_h = h).  inds/scores may be NULL.
+ * gate_dtype: dtype of W_gate.
+ * Replaces: SeedlessMetal.encodeMoEBlock (SeedlessMetal.swift:576-609). */
+int momij_moe_block(void* h, const void* norm_w, float eps, const void* w_gate, int gate_dtype,
+                    const uint32_t* w_ug, const void* s_ug, const void* b_ug, const uint32_t* w_dn,
+                    const void* s_dn, const void* b_dn, int32_t* inds, float* scores, int M, int H,
+                    int I, int E, int Ktop, int gs, float clamp, int dtype, void* workspace,
+                    size_t workspace_bytes, momij_stream_t stream);
+
 /* Expert-parallel decode (experts sharded contiguously: rank r owns experts
  * [r*E/world, (r+1)*E/world)).  The caller runs the two all-to-all exchanges
  * with its own NCCL communicator (ncclSend/ncclRecv or all-to-all of equal

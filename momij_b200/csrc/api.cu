@@ -1072,6 +1072,118 @@ int momij_moe_permute(const int32_t* inds, const float* scores, int M, int K, in
                               pair, weight, static_cast<int32_t*>(nullptr)));
 }
 
+namespace {
+using GateFn = void (*)(const uint16_t*, const uint16_t*, float*, int, int, int);
+using RouterFn = void (*)(const uint16_t*, const uint16_t*, unsigned*, float*, int32_t*, float*, int, int, int,
+                          int);
+GateFn pick_gate(int xt, int wt) {
+    if (xt == MOMIJ_DTYPE_BF16)
+        return wt == MOMIJ_DTYPE_BF16 ? gate_gemv_kernel<MOMIJ_DTYPE_BF16, MOMIJ_DTYPE_BF16>
+                                      : gate_gemv_kernel<MOMIJ_DTYPE_BF16, MOMIJ_DTYPE_F16>;
+    return wt == MOMIJ_DTYPE_BF16 ? gate_gemv_kernel<MOMIJ_DTYPE_F16, MOMIJ_DTYPE_BF16>
+                                  : gate_gemv_kernel<MOMIJ_DTYPE_F16, MOMIJ_DTYPE_F16>;
+}
+RouterFn pick_router(int xt, int wt) {
+    if (xt == MOMIJ_DTYPE_BF16)
+        return wt == MOMIJ_DTYPE_BF16 ? fused_router_kernel<MOMIJ_DTYPE_BF16, MOMIJ_DTYPE_BF16>
+                                      : fused_router_kernel<MOMIJ_DTYPE_BF16, MOMIJ_DTYPE_F16>;
+    return wt == MOMIJ_DTYPE_BF16 ? fused_router_kernel<MOMIJ_DTYPE_F16, MOMIJ_DTYPE_BF16>
+                                  : fused_router_kernel<MOMIJ_DTYPE_F16, MOMIJ_DTYPE_F16>;
+}
+bool dtype_ok(int dt) { return dt == MOMIJ_DTYPE_BF16 || dt == MOMIJ_DTYPE_F16; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int launch_gate(const void* x, const void* w, float* logits, int M, int H, int E, int xt, int wt,
+                cudaStream_t st) {
+    const int warps = 8;
+    return cuda_status(launch(pick_gate(xt, wt), dim3((E + warps - 1) / warps, (M + 7) / 8), dim3(32 * warps), 0,
+                              st, static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(w), logits, M, H,
+                              E));
+}
+}  // namespace
+
+int momij_moe_router_logits(const void* x, const void* w_gate, float* logits, int M, int H, int E,
+                            int x_dtype, int w_dtype, momij_stream_t stream) {
+    if (int rc = check_device()) return rc;
+    if (!x || !w_gate || !logits || M < 0 || H < 1 || E < 1 || !dtype_ok(x_dtype) || !dtype_ok(w_dtype))
+        return MOMIJ_ERR_INVALID_ARGUMENT;
+    if (H % 256 || !aligned16(x) || !aligned16(w_gate)) return MOMIJ_ERR_UNSUPPORTED_SHAPE;
+    if (M == 0) return MOMIJ_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int slot = prof_begin(MOMIJ_KERNEL_PLAN, st);
+    const int rc = launch_gate(x, w_gate, logits, M, H, E, x_dtype, w_dtype, st);
+    prof_end(slot, st);
+    return rc;
+}
+
+int momij_moe_fused_router(const void* x, const void* w_gate, uint32_t* counter, float* logits,
+                           int32_t* inds, float* scores, int M, int H, int E, int K, int x_dtype,
+                           int w_dtype, momij_stream_t stream) {
+    if (int rc = check_device()) return rc;
+    if (!x || !w_gate || !counter || !logits || !inds || !scores || M < 0 || H < 1 || E < 1 || K < 1 ||
+        !dtype_ok(x_dtype) || !dtype_ok(w_dtype))
+        return MOMIJ_ERR_INVALID_ARGUMENT;
+    if (H % 256 || E % 8 || K > 32 || K > E || M > 64 || E > 8192 || !aligned16(x) || !aligned16(w_gate))
+        return MOMIJ_ERR_UNSUPPORTED_SHAPE;
+    if (M == 0) return MOMIJ_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    RouterFn fn = pick_router(x_dtype, w_dtype);
+    const size_t smem = sizeof(float) * (size_t)E;
+    if (smem > 48 * 1024 && cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+                                cudaSuccess)
+        return MOMIJ_ERR_CUDA;
+    const int slot = prof_begin(MOMIJ_KERNEL_PLAN, st);
+    const int rc = cuda_status(launch(fn, dim3(E / 8), dim3(256), smem, st, static_cast<const uint16_t*>(x),
+                                      static_cast<const uint16_t*>(w_gate), reinterpret_cast<unsigned*>(counter),
+                                      logits, inds, scores, M, H, E, K));
+    prof_end(slot, st);
+    return rc;
+}
+
+int momij_rms_norm(const void* x, const void* w, void* out, int M, int H, float eps, int dtype,
+                   momij_stream_t stream) {
+    if (int rc = check_device()) return rc;
+    if (!x || !w || !out || M < 0 || H < 1 || !dtype_ok(dtype)) return MOMIJ_ERR_INVALID_ARGUMENT;
+    if (M == 0) return MOMIJ_OK;
+    auto fn = dtype == MOMIJ_DTYPE_BF16 ? rms_norm_kernel<MOMIJ_DTYPE_BF16> : rms_norm_kernel<MOMIJ_DTYPE_F16>;
+    return cuda_status(launch(fn, dim3(M), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                              static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(w),
+                              static_cast<uint16_t*>(out), H, eps));
+}
+
+size_t momij_moe_block_workspace_size(int M, int Ktop, int H, int I, int E) {
+    if (M < 0 || Ktop < 1 || H < 0 || I < 0 || E < 1) return 0;
+    return carve(nullptr, M, Ktop, H, I).bytes + align_up((size_t)M * H * 2, 256) + align_up((size_t)M * E * 4, 256);
+}
+
+int momij_moe_block(void* h, const void* norm_w, float eps, const void* w_gate, int gate_dtype,
+                    const uint32_t* w_ug, const void* s_ug, const void* b_ug, const uint32_t* w_dn,
+                    const void* s_dn, const void* b_dn, int32_t* inds, float* scores, int M, int H,
+                    int I, int E, int Ktop, int gs, float clamp, int dtype, void* workspace,
+                    size_t workspace_bytes, momij_stream_t stream) {
+    if (int rc = check_device()) return rc;
+    if (!h || !norm_w || !w_gate || !workspace || M < 0 || !dtype_ok(gate_dtype) || !dtype_ok(dtype))
+        return MOMIJ_ERR_INVALID_ARGUMENT;
+    if (M == 0) return MOMIJ_OK;
+    if (workspace_bytes < momij_moe_block_workspace_size(M, Ktop, H, I, E)) return MOMIJ_ERR_WORKSPACE;
+    if (H % 256 || !aligned16(h) || !aligned16(w_gate)) return MOMIJ_ERR_UNSUPPORTED_SHAPE;
+    const size_t base = carve(nullptr, M, Ktop, H, I).bytes;
+    unsigned char* tail = static_cast<unsigned char*>(workspace) + base;
+    void* xn = tail;
+    float* logits = reinterpret_cast<float*>(tail + align_up((size_t)M * H * 2, 256));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (int rc = momij_rms_norm(h, norm_w, xn, M, H, eps, dtype, stream)) return rc;
+    int rc;
+    {
+        const int slot = prof_begin(MOMIJ_KERNEL_PLAN, st);
+        rc = launch_gate(xn, w_gate, logits, M, H, E, dtype, gate_dtype, st);
+        prof_end(slot, st);
+    }
+    if (rc) return rc;
+    return momij_moe_forward(logits, xn, w_ug, s_ug, b_ug, w_dn, s_dn, b_dn, inds, scores, nullptr, h, M, H, I, E,
+                             Ktop, gs, clamp, dtype, workspace, base, stream);
+}
+
 size_t momij_moe_workspace_size(int M, int Ktop, int H, int I) {
     if (M < 0 || Ktop < 1 || H < 0 || I < 0) return 0;
     return carve(nullptr, M, Ktop, H, I).bytes;

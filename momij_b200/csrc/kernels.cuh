@@ -57,4 +57,13 @@ __global__ void ep_combine_kernel(const uint16_t* back, const float* scores, con
 __global__ void synth_fill_kernel(void* dst, int64_t n, int kind, float a, float c, uint64_t seed,
                                   uint64_t stream_id, int64_t start, int dtype);
 
+// block.cu: router gate GEMV, fused router, RMSNorm
+template <int XT, int WT>
+__global__ void gate_gemv_kernel(const uint16_t* x, const uint16_t* w, float* logits, int M, int H, int E);
+template <int XT, int WT>
+__global__ void fused_router_kernel(const uint16_t* x, const uint16_t* w, unsigned* ctr, float* logits,
+                                    int32_t* inds, float* scores, int M, int H, int E, int K);
+template <int DT>
+__global__ void rms_norm_kernel(const uint16_t* x, const uint16_t* w, uint16_t* out, int H, float eps);
+
 }  // namespace momij

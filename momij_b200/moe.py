@@ -68,6 +68,12 @@ def _load() -> ctypes.CDLL:
     L.momij_moe_ep_combine.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, vp, vp]
     L.momij_synth_fill.argtypes = [vp, ctypes.c_int64, i, f, f, ctypes.c_uint64,
                                    ctypes.c_uint64, ctypes.c_int64, i, vp]
+    L.momij_moe_router_logits.argtypes = [vp, vp, vp, i, i, i, i, i, vp]
+    L.momij_moe_fused_router.argtypes = [vp] * 6 + [i] * 6 + [vp]
+    L.momij_rms_norm.argtypes = [vp, vp, vp, i, i, f, i, vp]
+    L.momij_moe_block_workspace_size.argtypes = [i, i, i, i, i]
+    L.momij_moe_block_workspace_size.restype = sz
+    L.momij_moe_block.argtypes = [vp, vp, f, vp, i] + [vp] * 8 + [i] * 6 + [f, i, vp, sz, vp]
     L.momij_set_stop_flag.argtypes = [vp]
     L.momij_set_spin_limit.argtypes = [i]
     L.momij_profile_enable.argtypes = [i]
@@ -338,3 +344,65 @@ class MoELayer:
         return expert_ffn(x, self.wts, inds, scores, y, H=self.H, I=self.I, Ktop=self.Ktop,
                           gs=self.gs, M=M, clamp=self.clamp, workspace=self.workspace,
                           stream=stream)
+
+
+# ---- router GEMV, fused router, RMSNorm, MoE block ---------------------------
+
+def router_logits(x: torch.Tensor, w_gate: torch.Tensor, logits: torch.Tensor | None = None, *,
+                  stream=None) -> torch.Tensor:
+    """logits [M, E] (fp32) = x [M, H] @ w_gate [E, H]^T (maple_batched_gemv)."""
+    M, H = x.shape
+    E = w_gate.shape[0]
+    if logits is None:
+        logits = torch.empty(M, E, dtype=torch.float32, device=x.device)
+    _check(lib.momij_moe_router_logits(_ptr(x), _ptr(w_gate), _ptr(logits), M, H, E, _dtype_code(x),
+                                       _dtype_code(w_gate), _stream(stream)), "router_logits")
+    return logits
+
+
+def fused_router(x: torch.Tensor, w_gate: torch.Tensor, K: int, counter: torch.Tensor, *, logits=None,
+                 inds=None, scores=None, stream=None):
+    """MapleFused.fusedRouter: gate GEMV + softmax + top-K + renormalisation in
+    one launch; ``counter`` is a persistent zeroed int32/uint32 device word."""
+    M, H = x.shape
+    E = w_gate.shape[0]
+    dev = x.device
+    logits = torch.empty(M, E, dtype=torch.float32, device=dev) if logits is None else logits
+    inds = torch.empty(M, K, dtype=torch.int32, device=dev) if inds is None else inds
+    scores = torch.empty(M, K, dtype=torch.float32, device=dev) if scores is None else scores
+    _check(lib.momij_moe_fused_router(_ptr(x), _ptr(w_gate), _ptr(counter), _ptr(logits), _ptr(inds),
+                                      _ptr(scores), M, H, E, K, _dtype_code(x), _dtype_code(w_gate),
+                                      _stream(stream)), "fused_router")
+    return inds, scores
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | None = None, *,
+             stream=None) -> torch.Tensor:
+    """maple_rms_norm: out = round((x * rsqrt(mean(x^2) + eps)) * w)."""
+    M, H = x.shape
+    out = torch.empty_like(x) if out is None else out
+    _check(lib.momij_rms_norm(_ptr(x), _ptr(w), _ptr(out), M, H, float(eps), _dtype_code(x), _stream(stream)),
+           "rms_norm")
+    return out
+
+
+def block_workspace_size(M: int, Ktop: int, H: int, I: int, E: int) -> int:
+    return int(lib.momij_moe_block_workspace_size(M, Ktop, H, I, E))
+
+
+def moe_block(h: torch.Tensor, norm_w: torch.Tensor, eps: float, w_gate: torch.Tensor, wts: dict, *,
+              I: int, Ktop: int, gs: int = 64, clamp: float = 7.0, inds=None, scores=None, workspace=None,
+              stream=None) -> torch.Tensor:
+    """SeedlessMetal.encodeMoEBlock: h += MoE(rmsnorm(h)) in place (gate GEMV,
+    top-K routing, experts with the fused score-residual rounding)."""
+    M, H = h.shape
+    E = w_gate.shape[0]
+    need = block_workspace_size(M, Ktop, H, I, E)
+    if workspace is None:  # zeroed: completion counters and barrier words start at zero
+        workspace = torch.zeros(need, dtype=torch.uint8, device=h.device)
+    _check(lib.momij_moe_block(_ptr(h), _ptr(norm_w), float(eps), _ptr(w_gate), _dtype_code(w_gate),
+                               _ptr(wts["w_ug"]), _ptr(wts["s_ug"]), _ptr(wts["b_ug"]), _ptr(wts["w_dn"]),
+                               _ptr(wts["s_dn"]), _ptr(wts["b_dn"]), _ptr(inds), _ptr(scores), M, H, I, E,
+                               Ktop, gs, float(clamp), _dtype_code(h), _ptr(workspace), workspace.numel(),
+                               _stream(stream)), "moe_block")
+    return h

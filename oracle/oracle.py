@@ -276,3 +276,83 @@ def np_expert_ffn(x, wts, inds, scores, M, H, I, Ktop, gs, clamp=7.0, dtype=0):
     d = np_half_to_f64(dn, dtype).reshape(M, Ktop, H)
     y = (d * np.asarray(scores, np.float64).reshape(M, Ktop, 1)).sum(axis=1)
     return np_f64_to_half(y, dtype), {"ug": ug, "act": act, "down": dn}
+
+
+# ---- router GEMV, fused router, RMSNorm (numpy restatements) --------------
+
+def gate_logits(x, w_gate, x_dtype: int = 0, w_dtype: int = 0) -> np.ndarray:
+    """Router logits [M, E] = x [M, H] W_gate [E, H]^T from the 16-bit bit
+    patterns, in float64 (every product exact, the sum to ~2^-50):
+    maple_batched_gemv / maple_gate_gemv (SeedlessMetal.swift:2542-2595)
+    without their fp32 rounding."""
+    return np_half_to_f64(x, x_dtype) @ np_half_to_f64(w_gate, w_dtype).T
+
+
+def _f32(v):
+    return np.float32(v)
+
+
+def fused_router(logits_f32: np.ndarray, K: int):
+    """MapleFused.fusedRouter's selection and scores (MapleFused.swift:
+    139-240) on given fp32 logits, with its fp32 staging and summation order:
+    max; e_j = exp(l_j - max); the sum per thread t over j = t, t+256, ...,
+    then a 32-lane shuffle-down tree, then the eight simdgroups in order;
+    p_j = e_j * (1 / (sum + 1e-20)); top-K over p with the scan's tie order
+    (lower simdgroup, then smaller bit-reversed lane, then lower j within a
+    thread); scores p_k / (sum_k p_k + 1e-20), the sum in selection order.
+    Pure Python loops over E: small cases only."""
+    lg = np.asarray(logits_f32, np.float32)
+    M, E = lg.shape
+    inds = np.zeros((M, K), np.int32)
+    scores = np.zeros((M, K), np.float32)
+
+    def rev5(v):
+        return int(f"{v:05b}"[::-1], 2)
+
+    for m in range(M):
+        row = lg[m]
+        mx = _f32(row.max())
+        ev = np.exp((row - mx).astype(np.float64)).astype(np.float32)
+        part = [np.float32(0)] * 256
+        for t in range(256):
+            acc = np.float32(0)
+            for j in range(t, E, 256):
+                acc = _f32(acc + ev[j])
+            part[t] = acc
+        sg_sums = []
+        for sg in range(8):
+            lane = [part[sg * 32 + l] for l in range(32)]
+            off = 16
+            while off >= 1:
+                for l in range(32 - off):
+                    lane[l] = _f32(lane[l] + lane[l + off])
+                off //= 2
+            sg_sums.append(lane[0])
+        tot = sg_sums[0]
+        for v in sg_sums[1:]:
+            tot = _f32(tot + v)
+        inv = _f32(np.float32(1.0) / _f32(tot + np.float32(1e-20)))
+        p = (ev * inv).astype(np.float32)
+        key = [(-float(p[j]), ((j & 255) >> 5), rev5(j & 31), j) for j in range(E)]
+        order = sorted(range(E), key=lambda j: key[j])[:K]
+        sel = [p[j] for j in order]
+        ssum = np.float32(0)
+        for v in sel:
+            ssum = _f32(ssum + v)
+        inds[m] = order
+        scores[m] = [_f32(v / _f32(ssum + np.float32(1e-20))) for v in sel]
+    return inds, scores
+
+
+def rms_norm(x, w, eps: float, dtype: int = 0) -> np.ndarray:
+    """maple_rms_norm (SeedlessMetal.swift:2496-2527): inv = 1/sqrt(sum x^2 / H
+    + eps) (here from a float64 sum, rounded to fp32), out = round((x * inv)
+    * w) with both products rounded to fp32, then to the 16-bit dtype."""
+    xf = np_half_to_f64(x, dtype)
+    wf = np_half_to_f64(w, dtype)
+    H = xf.shape[1]
+    ss = (xf * xf).sum(axis=1)
+    inv = (1.0 / np.sqrt((ss / H).astype(np.float32).astype(np.float64) + np.float32(eps))).astype(np.float32)
+    t = (xf.astype(np.float32) * inv[:, None]).astype(np.float32)
+    o = (t * wf.astype(np.float32)).astype(np.float32)
+    return np_f64_to_half(o.astype(np.float64), dtype)
