@@ -163,6 +163,31 @@ def test_gqmm2_matches_oracle(M, Ktop, K, N, E, gs, dt, lhs):
     assert_parity(host16(out), ref, dt, "gqmm2")
 
 
+@pytest.mark.parametrize("M,K,N", [
+    (1, 2048, 3072),   # QKV of a 2048-wide model (q 2048, k and v 512 each)
+    (8, 2048, 2048),   # O projection, verify batch
+    (1, 4096, 6144),   # QKV at hidden 4096
+    (4, 4096, 4096),   # O at hidden 4096
+])
+def test_dense_projection_ktop1(M, K, N):
+    """The dense 2-bit projections of attention reuse gqmm2 with one "expert"
+    and Ktop = 1 (SeedlessMetal.swift:951-952, 1001-1002: inds all zero,
+    lhsPerExpert false)."""
+    gs, dt = 64, 0
+    w = S.codes(N * K // 16, 2, 110).reshape(1, N, K // 16)
+    s = S.affine_uniform(N * K // gs, S.SCALE_A, S.SCALE_C, 2, 111, dt).reshape(1, N, K // gs)
+    b = S.affine_uniform(N * K // gs, S.BIAS_A, S.BIAS_C, 2, 112, dt).reshape(1, N, K // gs)
+    x = S.normal_half(M * K, 2, 113, dt).reshape(M, K)
+    inds = np.zeros((M, 1), np.int32)
+    ref = O.gqmm2(x, w, s, b, inds, M, 1, K, N, gs, False, dt)
+    out = torch.empty(M, N, dtype=TD[dt], device=DEV)
+    ws = moe.new_workspace(M, 1, 0, 0)
+    moe.gqmm2(dev16(x, dt), torch.from_numpy(w.view(np.int32)).to(DEV), dev16(s, dt), dev16(b, dt),
+              torch.from_numpy(inds).to(DEV), out, Ktop=1, K=K, N=N, gs=gs, M=M, workspace=ws)
+    moe.synchronize(workspace=ws)
+    assert_parity(host16(out), ref, dt, "dense gqmm2")
+
+
 def test_gqmm2_repeated_expert_in_token():
     """gqmm2 callers may repeat an expert inside a token (the reference test
     uses arbitrary inds); the plan splits such runs into more units."""
