@@ -546,15 +546,16 @@ def run_gpu(args, cfg) -> None:
 
 def run_ep(args, cfg) -> None:
     """Config 4: M tokens per step split evenly over the ranks (each rank owns
-    M/N sequences and E/N experts); per layer route -> dispatch -> all-to-all
-    -> local experts -> all-to-all -> combine (momij_b200/ep.py).  Strong
-    scaling: the total work per step is fixed as N grows.  On one GPU the
-    step is the plain single-GPU layer (moe.forward), the best one-GPU path."""
+    M/N sequences and E/N experts); per layer route -> momij_moe_ep_forward
+    (the C-ABI expert-parallel layer: dispatch -> NCCL send/recv of the
+    destination segments -> local experts -> send/recv back -> combine).
+    Strong scaling: the total work per step is fixed as N grows.  On one GPU
+    the step is the plain single-GPU layer (moe.forward), the best one-GPU
+    path."""
     import torch
     world, rank, local = dist_setup()
     torch.cuda.set_device(local)
     from momij_b200 import moe, synth as S
-    from momij_b200.ep import ExpertParallelMoE, GpuOps
 
     H, I, E, K, gs, M, L = (cfg[k] for k in ("H", "I", "E", "K", "gs", "M", "L"))
     if M % world or E % world:
@@ -570,8 +571,12 @@ def run_ep(args, cfg) -> None:
     logits = torch.from_numpy(lg_host).to(dev)
     h = torch.from_numpy(x_host.view(np.int16)).to(dev).view(torch.bfloat16)
     stream = torch.cuda.Stream(device=dev)
-    ops = GpuOps(W[0], H=H, I=I, gs=gs, stream=stream)
-    layer = ExpertParallelMoE(ops, E=E, H=H, I=I, K=K, M=Ml, device=dev)
+    eplayer = None
+    if world > 1:  # one NCCL communicator for the layer object, from rank 0's unique id
+        import torch.distributed as dist
+        uid = [moe.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        eplayer = moe.EpLayer(rank=rank, world=world, E=E, H=H, I=I, K=K, max_tokens=Ml, gs=gs, unique_id=uid[0])
     ws = moe.new_workspace(Ml, K, H, I, dev)
     inds_all = torch.empty(L, Ml, K, dtype=torch.int32, device=dev)
     scores_all = torch.empty(L, Ml, K, dtype=torch.float32, device=dev)
@@ -582,15 +587,16 @@ def run_ep(args, cfg) -> None:
                 moe.forward(logits[l], h, W[l], None, H=H, I=I, Ktop=K, gs=gs, M=Ml, inds=inds_all[l],
                             scores=scores_all[l], resid_h=h, workspace=ws, stream=stream)
             else:
-                ops.w = W[l]
-                layer.inds, layer.scores = inds_all[l], scores_all[l]
-                layer.forward(logits[l], h)
+                moe.route(logits[l], K, inds_all[l], scores_all[l], stream=stream)
+                eplayer.forward(h, W[l], inds=inds_all[l], scores=scores_all[l], resid_h=h, stream=stream)
 
     with torch.cuda.stream(stream):
         step()
     torch.cuda.synchronize()
-    if int(layer.status.item()) != 0:
-        raise SystemExit(f"ep status {int(layer.status.item())}")
+    if eplayer is not None:
+        eplayer.status(stream)
+    else:
+        moe.synchronize(stream, ws)
     # algorithmic bytes of this rank: its experts that the step's tokens select
     ih = inds_all.cpu().numpy()
     if world > 1:  # every rank's routing, to count the local experts used
@@ -690,6 +696,38 @@ def run_ep(args, cfg) -> None:
     if world > 1:  # dispatch + combine gathers/kernels beside the instrumented ones
         launches += 3 * L
 
+    # --- parity (after the timed region): layer 0 of this rank's first tokens
+    # from the initial activations, y = MoE(x), against the oracle; the worst
+    # row and whether every rank's router indices match, over all ranks
+    nchk = min(Ml, 8)
+    x0 = torch.from_numpy(np.ascontiguousarray(x_host[:nchk]).view(np.int16)).to(dev).view(torch.bfloat16)
+    y0 = torch.empty(nchk, H, dtype=torch.bfloat16, device=dev)
+    i0 = torch.empty(Ml, K, dtype=torch.int32, device=dev)
+    s0 = torch.empty(Ml, K, dtype=torch.float32, device=dev)
+    with torch.cuda.stream(stream):
+        moe.route(logits[0][:nchk].contiguous(), K, i0[:nchk], s0[:nchk], stream=stream)
+        if world == 1:
+            moe.forward(logits[0][:nchk].contiguous(), x0, W[0], y0, H=H, I=I, Ktop=K, gs=gs, M=nchk,
+                        workspace=ws, stream=stream)
+        else:
+            eplayer.forward(x0, W[0], inds=i0[:nchk], scores=s0[:nchk], y=y0, stream=stream)
+    if eplayer is not None:
+        eplayer.status(stream)
+    else:
+        moe.synchronize(stream, ws)
+    pr = oracle_check(cfg, W[0], lg_host[0][:nchk], x_host[:nchk],
+                      y0.view(torch.int16).cpu().numpy().view(np.uint16), i0[:nchk].cpu().numpy(), expert_lo=lo)
+    pv = torch.tensor([pr["max_rel_l2"], 1.0 if pr["idx_exact"] else 0.0], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        mx = pv[:1].clone()
+        mn = pv[1:].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        dist.all_reduce(mn, op=dist.ReduceOp.MIN)
+        pv = torch.cat([mx, mn])
+    parity = {"tokens": nchk * world, "ranks": world, "max_rel_l2": float(pv[0].item()),
+              "idx_exact": bool(pv[1].item() == 1.0), "tol": 2e-3}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         wh, xh, ihh, sh = host_layer_inputs(cfg, 0)
@@ -719,6 +757,7 @@ def run_ep(args, cfg) -> None:
                                                           / max(kt[moe.KERNEL_COMBINE][1], 1)),
                                            "layer": _us(kt[moe.KERNEL_LAYER][0] / max(kt[moe.KERNEL_LAYER][1], 1))}},
             "launches_per_layer": {str(k): v[1] / L for k, v in kt.items()},
+            "parity": parity,
             "clocks": clocks,
             "e2e": {"value": e2e_tok_s, "unit": "tokens/s", "h2d_bytes_per_step": x_pin.numel() * 2
                     + lg_pin.numel() * 4, "d2h_bytes_per_step": y_pin.numel() * 2,
@@ -728,6 +767,9 @@ def run_ep(args, cfg) -> None:
         }
         print(json.dumps(line), flush=True)
     del graph
+    if eplayer is not None:
+        torch.cuda.synchronize()
+        eplayer.close()
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

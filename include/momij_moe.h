@@ -275,6 +275,37 @@ int momij_moe_ep_combine(const void* back, const float* scores, const int32_t* s
                          void* resid_h, int M, int K, int H, int dtype, const int32_t* status,
                          momij_stream_t stream);
 
+/* Expert-parallel layer object: the communicator and the exchange buffers of
+ * one rank (sized for max_tokens tokens of K slots per call).
+ *   momij_moe_ep_init: nccl_comm points to the caller's ncclComm_t (world
+ *     ranks, this GPU current), or is NULL and unique_id (the 128 bytes of a
+ *     ncclUniqueId, e.g. from momij_nccl_unique_id on rank 0, shared by the
+ *     caller) makes a communicator owned by the object; world == 1 needs
+ *     neither.  E % world == 0, max_tokens*K + 1 <= H/2 and
+ *     world*(max_tokens*K + 1) <= MOMIJ_MAX_PAIRS.
+ *   momij_moe_ep_forward: one MoE layer for this rank's M <= max_tokens
+ *     tokens: routing from logits [M,E] (or the given inds/scores when logits
+ *     is NULL), dispatch, exchange, the rank's experts (w_* hold experts
+ *     [rank*E/world, (rank+1)*E/world)), exchange back, combine into y or
+ *     resid_h -- the same bits as the single-GPU path.  Enqueued on `stream`
+ *     only (no host synchronisation; capturable in a CUDA graph); every rank
+ *     calls it with the same M.
+ *   momij_moe_ep_status: synchronises `stream` and returns the layer's
+ *     status (expert index, workspace or timeout errors of its kernels).
+ * NCCL is loaded at run time (libnccl.so.2); MOMIJ_ERR_NCCL when missing.
+ * Replaces: no counterpart in the reference (one GPU); the exchange sequence
+ * of north-star config 4 behind one call, for a caller without Python. */
+typedef struct momij_ep momij_ep_t;
+int momij_nccl_unique_id(void* out_128_bytes);
+int momij_moe_ep_init(void* nccl_comm, const void* unique_id, int rank, int world, int E, int H, int I,
+                      int K, int max_tokens, int gs, float clamp, int dtype, momij_ep_t** out);
+int momij_moe_ep_forward(momij_ep_t* ep, const float* logits, const int32_t* inds, const float* scores,
+                         const void* x, const uint32_t* w_ug, const void* s_ug, const void* b_ug,
+                         const uint32_t* w_dn, const void* s_dn, const void* b_dn, void* y, void* resid_h,
+                         int M, momij_stream_t stream);
+int momij_moe_ep_status(momij_ep_t* ep, momij_stream_t stream);
+int momij_moe_ep_destroy(momij_ep_t* ep);
+
 /* Per-kernel GPU timing.  While enabled, each launch made by the entry points
  * above is bracketed by two CUDA events on its stream (also when the stream
  * is being captured into a CUDA graph; the pair then times the latest replay).

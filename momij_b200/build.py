@@ -20,7 +20,8 @@ CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(HERE, "_build")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libmomij_moe.so")
-SOURCES = ["route.cu", "gemv.cu", "layer.cu", "decode.cu", "block.cu", "prefill.cu", "ep.cu", "misc.cu", "api.cu", "noalloc.cu"]
+SOURCES = ["route.cu", "gemv.cu", "layer.cu", "decode.cu", "block.cu", "prefill.cu", "ep.cu", "ep_host.cu", "misc.cu",
+           "api.cu", "noalloc.cu"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -65,7 +66,7 @@ def build(jobs: int = 4, verbose_ptxas: bool = False) -> str:
         objs = list(ex.map(lambda s: _compile(s, verbose_ptxas), SOURCES))
     if (not os.path.exists(LIB) or
             os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs)):
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-cudart", "static",
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-cudart", "static", "-ldl",
                                                                   "-ccbin", "/usr/bin/g++"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:

@@ -662,6 +662,12 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
             const int nt = ph ? nt_dn : nt_up, nC = ph ? nC_dn : nC_up, nG = ph ? nG_dn : nG_up;
             const int4* tiles = ph ? S.tiles_dn : S.tiles_up;
             if (ph == 1) {
+                // the combine's completion counters start at zero whatever the
+                // workspace held (a call of another batch size carves it
+                // differently): CTA 0 clears them before the grid barrier that
+                // precedes every count
+                if (blockIdx.x == 0)
+                    for (int i = te; i < (a.H + 63) / 64; i += kDecEpiThreads) a.block_ctr[i] = 0u;
                 // act complete on every CTA: grid barrier, then the down phase's digits
                 __threadfence();
                 bar_sync(kBarEpi, kDecEpiThreads);

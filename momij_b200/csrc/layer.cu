@@ -373,6 +373,11 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
     stamp(a, 7);
 
     // ---- 3/4. down phase: its stages are already streaming --------------------
+    // the combine's completion counters start at zero whatever the workspace
+    // held (a call of another batch size carves it differently): CTA 0 clears
+    // them before the grid barrier that precedes every count
+    if (bx == 0)
+        for (int i = tid; i < (a.H + 63) / 64; i += kConsumerThreads) a.block_ctr[i] = 0u;
     const bool fine = layer_grid_barrier(a, true, &s_flag);
     if (!fine) {
         ring_quiesce();  // the down items issued before the barrier

@@ -1,6 +1,6 @@
 // tc.cuh -- sm_100a primitives: tensor memory (tcgen05.alloc/ld/st), the
 // tcgen05 MMA issued by one thread, TMA tensor loads into this CTA's shared
-// memory (no multicast), and bounded mbarrier waits.
+// memory (each load fills this CTA alone), and bounded mbarrier waits.
 #pragma once
 
 #include "common.cuh"

@@ -78,6 +78,10 @@ class ExpertParallelMoE:
         self.seg = self.capacity + 1
         if self.seg > H // 2:
             raise ValueError("the index row needs M*K + 1 <= H / 2")
+        if self.world * self.seg > moe.MAX_PAIRS:
+            # the experts step runs gqmm2 with one slot per received row
+            raise ValueError(f"world * (M*K + 1) = {self.world * self.seg} received rows exceeds "
+                             f"{moe.MAX_PAIRS} (MOMIJ_MAX_PAIRS): use fewer tokens per rank")
         rows = self.world * self.seg
         dev = device if device is not None else torch.device("cpu")
         self.inds = torch.empty(M, K, dtype=torch.int32, device=dev)
@@ -105,7 +109,22 @@ class ExpertParallelMoE:
                 out, inp = out.view(torch.int32), inp.view(torch.int32)
             dist.all_to_all_single(out, inp, group=self.group)
 
+    def check(self) -> None:
+        """Waits for the layer and raises SeedlessError if it failed: a bad
+        expert index or capacity overflow (the status word; the combine then
+        leaves h untouched) or an error of the experts' kernels."""
+        if self.status.is_cuda:
+            torch.cuda.current_stream(self.status.device).synchronize()
+        s = int(self.status.item())
+        if s != moe.OK:
+            raise moe.SeedlessError(s, "expertParallel")
+        if getattr(self.ops, "ws", None) is not None:
+            moe.synchronize(getattr(self.ops, "stream", None), self.ops.ws)
+
     def forward(self, logits, h):
+        """Enqueues one layer (no host synchronisation).  h is updated only
+        when the layer succeeds: call check() (or read `status`) before
+        trusting it."""
         o = self.ops
         o.route(logits, self.K, self.inds, self.scores)
         o.dispatch(self.inds, h, self.send_x, self.send_meta, self.slot_map, self.status, E=self.E,

@@ -224,6 +224,7 @@ def to_device(layer: dict, device="cuda") -> dict:
     for k, v in layer.items():
         if k in ("dtype", "gate_dtype"):
             continue
+        v = np.array(v)  # a writable copy (the store's arrays may be read-only maps)
         if k.startswith("w_"):
             out[k] = torch.from_numpy(v.view(np.int32)).to(device)
         else:

@@ -74,6 +74,11 @@ def _load() -> ctypes.CDLL:
     L.momij_moe_block_workspace_size.argtypes = [i, i, i, i, i]
     L.momij_moe_block_workspace_size.restype = sz
     L.momij_moe_block.argtypes = [vp, vp, f, vp, i] + [vp] * 8 + [i] * 6 + [f, i, vp, sz, vp]
+    L.momij_nccl_unique_id.argtypes = [vp]
+    L.momij_moe_ep_init.argtypes = [vp, vp] + [i] * 8 + [f, i, ctypes.POINTER(vp)]
+    L.momij_moe_ep_forward.argtypes = [vp] * 13 + [i, vp]
+    L.momij_moe_ep_status.argtypes = [vp, vp]
+    L.momij_moe_ep_destroy.argtypes = [vp]
     L.momij_set_stop_flag.argtypes = [vp]
     L.momij_set_spin_limit.argtypes = [i]
     L.momij_profile_enable.argtypes = [i]
@@ -406,3 +411,56 @@ def moe_block(h: torch.Tensor, norm_w: torch.Tensor, eps: float, w_gate: torch.T
                                Ktop, gs, float(clamp), _dtype_code(h), _ptr(workspace), workspace.numel(),
                                _stream(stream)), "moe_block")
     return h
+
+
+# ---- expert-parallel layer object (momij_moe_ep_*) ------------------------------
+
+def nccl_unique_id() -> bytes:
+    """128 bytes of a fresh ncclUniqueId (rank 0 makes it; every rank passes it
+    to EpLayer)."""
+    buf = ctypes.create_string_buffer(128)
+    _check(lib.momij_nccl_unique_id(buf), "ncclUniqueId")
+    return buf.raw
+
+
+class EpLayer:
+    """One rank of an expert-parallel MoE layer behind the C ABI: the
+    communicator (made from ``unique_id`` for world > 1) and the exchange
+    buffers for up to ``max_tokens`` tokens per call."""
+
+    def __init__(self, *, rank: int, world: int, E: int, H: int, I: int, K: int, max_tokens: int,
+                 gs: int = 64, clamp: float = 7.0, dtype=torch.bfloat16, unique_id: bytes | None = None):
+        self.E, self.H, self.I, self.K, self.world = E, H, I, K, world
+        code = DTYPE_BF16 if dtype == torch.bfloat16 else DTYPE_F16
+        uid = ctypes.create_string_buffer(unique_id, 128) if unique_id is not None else None
+        h = ctypes.c_void_p()
+        _check(lib.momij_moe_ep_init(None, uid, rank, world, E, H, I, K, max_tokens, gs, float(clamp), code,
+                                     ctypes.byref(h)), "epInit")
+        self._h = h
+
+    def forward(self, x: torch.Tensor, wts: dict, *, logits=None, inds=None, scores=None, y=None,
+                resid_h=None, stream=None):
+        """One layer for this rank's tokens x [M, H] with its local experts
+        ``wts``; y (or resid_h, updated in place) receives the result.  Call
+        ``status()`` before trusting the output."""
+        M = x.shape[0]
+        _check(lib.momij_moe_ep_forward(self._h, _ptr(logits), _ptr(inds), _ptr(scores), _ptr(x),
+                                        _ptr(wts["w_ug"]), _ptr(wts["s_ug"]), _ptr(wts["b_ug"]),
+                                        _ptr(wts["w_dn"]), _ptr(wts["s_dn"]), _ptr(wts["b_dn"]), _ptr(y),
+                                        _ptr(resid_h), M, _stream(stream)), "epForward")
+        return y if y is not None else resid_h
+
+    def status(self, stream=None) -> None:
+        """Synchronises the stream; raises SeedlessError on a failed layer."""
+        _check(lib.momij_moe_ep_status(self._h, _stream(stream)), "epStatus")
+
+    def close(self) -> None:
+        if self._h:
+            lib.momij_moe_ep_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -472,3 +472,24 @@ def test_large_batch_gemv_path_matches_oracle(M, H, I, E, K):
     # the GPU router's scores may differ from the oracle's in the last bit
     # (fp32 softmax), so this leg is held to the oracle tolerance
     assert_ffn_parity(host16(yd), y_ref, st["down"], scores, 0, f"large batch forward M={M}")
+
+
+def test_workspace_reuse_across_batch_sizes():
+    """One workspace for calls of different batch sizes (it is carved per
+    call, so a large call's buffers overlap a small call's counters): the
+    fused kernels clear their completion counters themselves."""
+    H, I, E, K, gs = 1024, 512, 32, 4, 64
+    wd = moe.device_expert_weights(E, H, I, gs, seed=3)
+    w = S.expert_weights(E, H, I, gs, seed=3)
+    ws = moe.new_workspace(64, K, H, I)
+    for M in (64, 8, 1, 64, 1):
+        x = S.activations(M, H, seed=M)
+        lg = S.logits_normal(M, E, 0, M)
+        y = torch.zeros(M, H, dtype=torch.bfloat16, device=DEV)
+        moe.forward(torch.from_numpy(lg).to(DEV), dev16(x, 0), wd, y, H=H, I=I, Ktop=K, gs=gs, M=M, workspace=ws)
+        moe.synchronize(workspace=ws)
+        i_ref, s_ref = O.route(lg, K)
+        ref, _ = O.expert_ffn(x, w, i_ref, s_ref, M, H, I, K, gs)
+        g, r = O.np_half_to_f64(host16(y)), O.np_half_to_f64(ref)
+        rel = np.sqrt(((g - r) ** 2).sum(1)) / np.sqrt((r ** 2).sum(1))
+        assert rel.max() <= 2e-3, (M, rel.max())
