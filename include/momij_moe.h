@@ -136,9 +136,12 @@ int momij_moe_gqmm2(const void* x, const uint32_t* w, const void* scales, const 
  * MOMIJ_NOALLOC_MAX_PAIRS, otherwise MOMIJ_ERR_WORKSPACE; every call shares
  * the array, so calls that overlap on the GPU race -- serialise them; the
  * first call on a device looks up the array's address (cudaGetSymbolAddress)
- * and should come before any stream capture on that device; an expert index
- * out of range makes the call write nothing to `out`, and this entry point
- * has no way to report it. */
+ * and should come before any stream capture on that device; the address is
+ * cached per device for the life of the process, so after cudaDeviceReset
+ * (or any other teardown of the device's primary context) the cached address
+ * is stale: do not call this entry point again in that process; an expert
+ * index out of range makes the call write nothing to `out`, and this entry
+ * point has no way to report it (the next valid call rewrites the plan). */
 #define MOMIJ_NOALLOC_MAX_PAIRS 1024
 int momij_moe_gqmm2_noalloc(const void* x, const uint32_t* w, const void* scales,
                             const void* biases, const int32_t* inds, void* out, int M, int Ktop,
