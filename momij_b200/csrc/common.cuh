@@ -182,26 +182,27 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
     return v;
 }
 
-// Grid barrier over gridDim.x co-resident CTAs by one thread: an arrival
+// Grid barrier over gridDim.x co-resident CTAs by one thread (after a
+// block barrier of the CTA's threads whose writes it publishes): an arrival
 // counter that the last arriver resets, and a generation word it then
-// increments; the others wait for the generation to change.  The counter
-// never exceeds the grid size and the generation is compared for change only,
-// so neither wraps into a wrong state.  Every CTA arrives even when it later
-// gives up waiting, so the counter is back at zero after every call.
-__device__ inline bool grid_barrier_thread(unsigned* arrive, unsigned* gen, int limit, bool wait) {
-    __threadfence();
-    const unsigned g0 = ld_acquire_u32(gen);
+// increments with release semantics; the others wait for the generation to
+// differ from g0, its value read when the kernel started (it cannot change
+// before this CTA arrives).  The counter never exceeds the grid size and the
+// generation is compared for change only, so neither wraps into a wrong
+// state.  Every CTA arrives even when it later gives up waiting, so the
+// counter is back at zero after every call.
+__device__ inline bool grid_barrier_thread(unsigned* arrive, unsigned* gen, unsigned g0, int limit, bool wait) {
+    __threadfence();  // the CTA's writes (ordered before this thread by the block barrier)
     const unsigned old = atomicAdd(arrive, 1u);
     if (old == gridDim.x - 1) {
         *reinterpret_cast<volatile unsigned*>(arrive) = 0u;  // no other CTA touches it before the generation moves
-        __threadfence();
-        atomicAdd(gen, 1u);
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(gen) : "memory");
         return true;
     }
     if (!wait) return false;
     for (int it = 0; it < limit; ++it) {
         if (ld_acquire_u32(gen) != g0) return true;
-        __nanosleep(64);
+        __nanosleep(32);
     }
     return ld_acquire_u32(gen) != g0;
 }

@@ -247,6 +247,7 @@ struct DecShared {
     int nan_tok[8];
     const uint16_t* vec_ptr[16];
     int nunits, bad, nt_up, nt_dn, udn0, nudn, nseg, nlast, flag, abort, stopped;
+    unsigned gen0;  // the grid barrier's generation before this call's round
     uint32_t tmem;
     alignas(8) uint64_t full[kDecMaxStages];
     alignas(8) uint64_t empty[kDecMaxStages];
@@ -316,6 +317,7 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
     pdl_launch_dependents();
     dstamp(a, 1);
     if (tid == 0 && a.stop && __ldcg(a.stop) != 0) S.stopped = 1;
+    if (tid == 0) S.gen0 = ld_acquire_u32(reinterpret_cast<const unsigned*>(a.ctrl + kCtrlGen));
     if (tid < 8) S.nan_tok[tid] = 0;
     __syncthreads();
     // A set stop flag (the reference's stopFlag, read once per CTA) skips the
@@ -669,14 +671,13 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                 if (blockIdx.x == 0)
                     for (int i = te; i < (a.H + 63) / 64; i += kDecEpiThreads) a.block_ctr[i] = 0u;
                 // act complete on every CTA: grid barrier, then the down phase's digits
-                __threadfence();
                 bar_sync(kBarEpi, kDecEpiThreads);
                 if (te == 0) dstamp_thread(a, 6);
                 if (te == 0) {
                     // every CTA arrives (also after an error), so the counter returns to zero
                     const bool wait = !*abort_flag;
                     S.flag = grid_barrier_thread(reinterpret_cast<unsigned*>(a.ctrl + kCtrlArrive),
-                                                 reinterpret_cast<unsigned*>(a.ctrl + kCtrlGen), a.spin_limit,
+                                                 reinterpret_cast<unsigned*>(a.ctrl + kCtrlGen), S.gen0, a.spin_limit,
                                                  wait) && wait;
                 }
                 bar_sync(kBarEpi, kDecEpiThreads);

@@ -46,12 +46,11 @@ __device__ __forceinline__ void stamp(const LayerArgs& a, int i) {
 
 // Grid barrier of the consumer threads (grid_barrier_thread by thread 0).
 // Every CTA arrives; `wait` false (this CTA already failed) arrives only.
-__device__ bool layer_grid_barrier(const LayerArgs& a, bool wait, int* s_flag) {
-    __threadfence();
+__device__ bool layer_grid_barrier(const LayerArgs& a, unsigned g0, bool wait, int* s_flag) {
     bar_sync(kBarConsumers, kConsumerThreads);
     if (threadIdx.x == 0) {
         const bool ok = grid_barrier_thread(reinterpret_cast<unsigned*>(a.ctrl + kCtrlArrive),
-                                            reinterpret_cast<unsigned*>(a.ctrl + kCtrlGen), a.spin_limit, wait) &&
+                                            reinterpret_cast<unsigned*>(a.ctrl + kCtrlGen), g0, a.spin_limit, wait) &&
                         wait;
         if (!ok) atomicExch(a.ctrl + kCtrlError, MOMIJ_ERR_TIMEOUT);
         __threadfence();
@@ -230,6 +229,7 @@ template <int DT, int GS, int TMAX, int STAGES>
 __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const LayerArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ int s_nunits, s_bad, s_flag, s_nlast, s_nseg, s_stopped;
+    __shared__ unsigned s_gen0;
     __shared__ int s_nan[8];
     __shared__ __align__(8) uint64_t s_sbar_up, s_sbar_dn;
     __shared__ int s_cnt_up[4], s_cnt_dn[4];
@@ -270,11 +270,16 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
     const int nlog = a.logits ? a.M * a.E : 0;
     const float lg0 = tid < nlog ? __ldcg(a.logits + tid) : 0.f;  // in flight during the encoding
     const int stop0 = (tid == 0 && a.stop) ? __ldcg(a.stop) : 0;
+    // the grid barrier's generation before this call's round (read early, off the critical path)
+    const unsigned gen0 = tid == 0 ? ld_acquire_u32(reinterpret_cast<const unsigned*>(a.ctrl + kCtrlGen)) : 0u;
     if (tid < a.M) up_tb.vecs[tid] = tid;
     if (tid < 8) s_nan[tid] = 0;
     __syncthreads();
     digitize<DT>(a.x, up_tb.vecs, a.M, a.H, s_dig, s_fs, kConsumerThreads);
-    if (tid == 0) s_stopped = stop0 != 0;
+    if (tid == 0) {
+        s_stopped = stop0 != 0;
+        s_gen0 = gen0;
+    }
     if (tid < nlog) {
         s_logits[tid] = lg0;
         if (isnan(lg0)) s_nan[tid / a.E] = 1;
@@ -378,7 +383,7 @@ __global__ void __launch_bounds__(kLayerThreads, 1) moe_layer_kernel(const Layer
     // them before the grid barrier that precedes every count
     if (bx == 0)
         for (int i = tid; i < (a.H + 63) / 64; i += kConsumerThreads) a.block_ctr[i] = 0u;
-    const bool fine = layer_grid_barrier(a, true, &s_flag);
+    const bool fine = layer_grid_barrier(a, s_gen0, true, &s_flag);
     if (!fine) {
         ring_quiesce();  // the down items issued before the barrier
         if (s_cnt_dn[0] > 0) dn.wait_sb();

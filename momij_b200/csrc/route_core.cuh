@@ -128,7 +128,10 @@ __device__ inline void route_tokens(const float* s_logits, const int* s_nan, int
                                     int E, int K, int t0, int nthr, int bar, int* s_inds, float* s_scores,
                                     long long* stamp_ranks = nullptr, bool with_scores = true) {
     const int t = threadIdx.x - t0;
-    constexpr int kParts = 8;  // threads per candidate
+    // threads per candidate: a power of two (<= 32) so that one pass covers
+    // every candidate when the threads suffice (at least 1)
+    int kParts = 1;
+    while (kParts < 32 && M * E * kParts * 2 <= nthr) kParts <<= 1;
     for (int base = 0; base < M * E * kParts; base += nthr) {
         const int it = base + t;
         const int c = it / kParts, sub = it % kParts;
@@ -146,7 +149,6 @@ __device__ inline void route_tokens(const float* s_logits, const int* s_nan, int
                 r += (lj > lc) | ((lj == lc) & (__brev((unsigned)j) < rc));
             }
         }
-#pragma unroll
         for (int o = 1; o < kParts; o <<= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
         if (valid && sub == 0 && !s_nan[m] && r < K) s_inds[m * K + r] = c - m * E;
     }
