@@ -402,7 +402,7 @@ int run_decode_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws,
     // start only after the routing)
     const size_t b_bytes = (size_t)std::max(nG_up, 2 * nG_dn) * dec_b_group_bytes(N);
     const size_t fs_bytes = align_up(8 * (size_t)std::max(c.M * nG_up, 2 * T * nG_dn), 16);
-    const size_t red_bytes = (size_t)2 * T * 128 * 4;
+    const size_t red_bytes = (size_t)4 * T * 128 * 4;  // one partial per MMA issuer
     const size_t lg_bytes = align_up(4 * (size_t)(c.logits ? c.M * c.E : 0), 16);
     const size_t fixed = align_up(b_bytes, 1024) + fs_bytes + red_bytes + 1024;
     int optin = 0, dev = 0;

@@ -393,7 +393,8 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
     auto wg_groups = [](int nG, int c, int d) { return min(4, max(0, min(8, nG - 8 * c) - 4 * d)); };
 
     if (warp >= kWarpMma0) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kDecRegsCtl));
-    else asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kDecRegsWork));
+    else if (warp < kWarpEpi0) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kDecRegsDeq));
+    else asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kDecRegsEpi));
     if (warp >= kWarpProd0 + kDecProducers) {
         // idle
     } else if (warp >= kWarpProd0) {
@@ -639,11 +640,13 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
         }
     } else {
         // ---- epilogue warpgroup d: warpgroup d's accumulators -> partial row sums ---
-        const int d = (warp - kWarpEpi0) >> 2, L = (warp & 3) * 32 + lane;
-        const int te = tid - kTidEpi0;  // 0 .. 255
+        // epilogue warp (d, hh, quarter): the accumulators of MMA issuer 2d + hh
+        const int ew = warp - kWarpEpi0, d = ew >> 3, hh = (ew >> 2) & 1, L = (warp & 3) * 32 + lane;
+        const int iw = 2 * d + hh;
+        const int te = tid - kTidEpi0;  // 0 .. kDecEpiThreads - 1
         const uint32_t lane_off = tmem_lane_base(warp);
         const uint32_t tD0 = tmem + d * 256 + 128;
-        int ude[2] = {0, 0}, item = 0;
+        int ude = 0, item = 0;
         bool oke = true;
         long long w_d = 0, cy_epi = 0;
         const bool prof = a.trace != nullptr && te == 0;
@@ -725,10 +728,10 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                     if (oke) oke = mbar_wait_warp(&S.full[s], (item / S_) & 1, a.spin_limit, abort_flag);
                     if (oke) {
                         const unsigned char* sbrow = s_ring + (size_t)s * kDecStageBytes + kDecCodeBytes + L * 16;
-                        if (GS == 64) {
-                            const uint2 sw = *reinterpret_cast<const uint2*>(sbrow + 8 * d);
-                            const uint2 bw = *reinterpret_cast<const uint2*>(sbrow + kDecSbBytes + 8 * d);
-                            sbw = make_uint4(sw.x, sw.y, bw.x, bw.y);
+                        if (GS == 64) {  // this warp's two groups 2hh, 2hh + 1 of warpgroup d's four
+                            const uint32_t sw = *reinterpret_cast<const uint32_t*>(sbrow + 8 * d + 4 * hh);
+                            const uint32_t bw = *reinterpret_cast<const uint32_t*>(sbrow + kDecSbBytes + 8 * d + 4 * hh);
+                            sbw = hh ? make_uint4(0u, sw, 0u, bw) : make_uint4(sw, 0u, bw, 0u);
                         } else {  // gs 128: two scales (one word) of the chunk's half of the box
                             const int so = 8 * (c & 1) + 4 * d;
                             sbw.x = *reinterpret_cast<const uint32_t*>(sbrow + so);
@@ -737,16 +740,14 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                     }
                     __syncwarp();
                     if (lane == 0 && oke) mbar_arrive(&S.empty[s]);
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        const int iw = 2 * d + hh;
+                    {
 #pragma unroll
                         for (int pk = 0; pk < 2 / GP; ++pk) {
-                            const int buf = ude[hh] % ND;
+                            const int buf = ude % ND;
                             const long long tw0 = a.trace ? gtime() : 0;
-                            if (oke) oke = mbar_wait_warp(&S.d_full[iw][buf], (ude[hh] / ND) & 1, a.spin_limit, abort_flag);
+                            if (oke) oke = mbar_wait_warp(&S.d_full[iw][buf], (ude / ND) & 1, a.spin_limit, abort_flag);
                             if (a.trace) w_d += gtime() - tw0;
-                            ++ude[hh];
+                            ++ude;
                             const long long cy0 = prof ? clock64() : 0;
                             if (oke) {
                                 tc_after_sync();
@@ -788,16 +789,16 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                         }
                     }
                 }
-                // ---- tile end: warpgroup partials -> (e0 + e1) -----------------------
+                // ---- tile end: the four issuers' partials -> (p00 + p01) + (p10 + p11) ----
 #pragma unroll
                 for (int v = 0; v < T; ++v)
-                    if ((vmask >> v) & 1) s_red[((size_t)d * T + v) * 128 + L] = acc[v];
+                    if ((vmask >> v) & 1) s_red[((size_t)iw * T + v) * 128 + L] = acc[v];
                 bar_sync(kBarEpi, kDecEpiThreads);
                 if (oke) {
                     const size_t st = (size_t)T * 128;
                     auto red_sum = [&](int v, int l) {
                         const float* r = s_red + (size_t)v * 128 + l;
-                        return r[0] + r[st];
+                        return (r[0] + r[st]) + (r[2 * st] + r[3 * st]);
                     };
                     if (ph == 0) {
                         for (int i = te; i < un.z * 64; i += kDecEpiThreads) {

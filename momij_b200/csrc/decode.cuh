@@ -17,27 +17,29 @@ constexpr int kCtrlStatus = 1, kCtrlError = 2, kCtrlArrive = 3, kCtrlGen = 4;
 // Warp roles of the decode kernel (20 warps):
 //   0-7   dequantise: warpgroup d (warps 4d..4d+3) turns the 16-code words of
 //         groups [4d, 4d+4) of every stage into the MMA's A operand in TMEM;
-//   8-15  epilogue: warpgroup d (warps 8+4d..) reads warpgroup d's
-//         accumulators (tcgen05.ld), applies the scales and biases (read from
-//         the stage, which both roles release), writes outputs;
-//   16-19 MMA issue (lane 0): warp 16+2d+h issues the MMAs of groups 2h, 2h+1
+//   8-23  epilogue: warp 8 + 8d + 4h + q reads the accumulators of MMA
+//         issuer (d, h) for TMEM lane quarter q (tcgen05.ld), applies the
+//         scales and biases (read from the stage, which both roles release),
+//         writes outputs;
+//   24-27 MMA issue (lane 0): warp 24+2d+h issues the MMAs of groups 2h, 2h+1
 //         of warpgroup d's four (a thread issues one MMA per ~60 cycles, and
 //         the issue rate grows with the number of issuing warps);
-//   20-21 TMA producers (lane 0), alternate stages; 22-23 idle.
+//   28-29 TMA producers (lane 0), alternate stages; 30-31 idle.
 constexpr int kDecDeqWarps = 8;
-constexpr int kDecEpiWarps = 8;
+constexpr int kDecEpiWarps = 16;
 constexpr int kDecMmaWarps = 4;
 constexpr int kDecProducers = 2;
 constexpr int kDecIdleWarps = 2;  // complete the producers' warpgroup (registers move per warpgroup)
 constexpr int kDecThreadsAll = 32 * (kDecDeqWarps + kDecEpiWarps + kDecMmaWarps + kDecProducers + kDecIdleWarps);
-// Registers per thread after the role split (setmaxnreg): the dequantising and
-// epilogue warpgroups take what the MMA / producer warpgroups give up; the sum
-// stays within the launch's 80 x kDecThreadsAll.
-constexpr int kDecRegsWork = 96, kDecRegsCtl = 40;
-static_assert(32 * (kDecDeqWarps + kDecEpiWarps) * kDecRegsWork +
+// Registers per thread after the role split (setmaxnreg): the epilogue
+// warpgroups take what the dequantising and the MMA / producer warpgroups give
+// up; the sum stays within the launch's 64 x kDecThreadsAll (1024 threads).
+constexpr int kDecRegsLaunch = 64, kDecRegsEpi = 80, kDecRegsDeq = 56, kDecRegsCtl = 40;
+static_assert(32 * kDecEpiWarps * kDecRegsEpi + 32 * kDecDeqWarps * kDecRegsDeq +
                       32 * (kDecMmaWarps + kDecProducers + kDecIdleWarps) * kDecRegsCtl <=
-                  80 * kDecThreadsAll,
+                  kDecRegsLaunch * kDecThreadsAll,
               "register split exceeds the launch's registers");
+static_assert(kDecThreadsAll == 1024, "one CTA of 1024 threads per SM");
 constexpr int kDecEpiThreads = 32 * kDecEpiWarps;
 constexpr int kDecRouteThreads = 32 * (kDecMmaWarps + kDecProducers);  // route while the others encode x
 constexpr int kDecCodeBytes = 128 * 128;   // a stage's codes: 128 rows x one 128-byte K chunk (8 groups)
