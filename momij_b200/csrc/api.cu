@@ -357,10 +357,17 @@ int run_decode_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws,
     const int N = dec_mma_n(T);
     const int nG_up = c.H / 64, nG_dn = c.I / 64;
     // tiles per CTA: rows of the slice / tile height, + 1 for a unit boundary
-    const long long rows_up = ((long long)P * c.I / 8 + G - 1) / G * 8;
-    const long long rows_dn = ((long long)P * c.H / 8 + G - 1) / G * 8;
+    // CTA slices weigh a unit's rows c0 + its tokens; the longest slice is then
+    // (c0 + T) / (c0 + 1) times the even one: c0 keeps it below one unit's
+    // rows (a down slice then spans at most two units) and within the tables
+    int c0 = 1;
+    const double even = (double)P / G;  // units per CTA at most, in unit lengths
+    while (c0 < 64 && (double)(c0 + T) / (c0 + 1) * even > 0.95) ++c0;
+    const double ratio = (double)(c0 + T) / (c0 + 1);
+    const long long rows_up = (long long)(((double)P * c.I / G) * ratio) + 8;
+    const long long rows_dn = (long long)(((double)P * c.H / G) * ratio) + 8;
     if (rows_up / 64 + 2 > kDecMaxTiles || rows_dn / 128 + 2 > kDecMaxTiles ||
-        rows_dn / 64 + 4 > kDecMaxLastBlocks)
+        rows_dn / 64 + 4 > kDecMaxLastBlocks || rows_dn > c.H)
         return kNotApplicable;
 
     // TMA row strides are multiples of 16 bytes: the scale rows (Kd / gs halves) too
@@ -395,6 +402,7 @@ int run_decode_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws,
     a.K = c.K;
     a.gs = gs;
     a.spin_limit = spin_limit();
+    a.slice_c0 = c0;
     a.clamp = c.clamp;
 
     // shared memory: ring of stages (codes + scales + biases) | B | per-group

@@ -77,6 +77,7 @@ __device__ void plan_units_warp(const int* s_inds, int P, int E, int K, int tmax
             const int e = s_inds[p];
             bad |= (e < 0 || e >= E);
             int less = 0, before = 0, same = 0;
+#pragma unroll 8
             for (int j = 0; j < P; ++j) {
                 const int ej = s_inds[j];
                 less += ej < e;
@@ -167,18 +168,32 @@ __device__ void digitize_b(const uint16_t* const* src, int nvec, int Kd, int N, 
     const int total = nvec * nG * 16;
     const int lane = threadIdx.x & 31;
     const int gbytes = dec_b_group_bytes(N);
+    // the next pass's four elements are loaded while this pass computes
+    auto load = [&](int bs, uint16_t (&raw)[4]) {
+        const int idx = bs + lane;
+        if (idx < total) {
+            const int vg = idx >> 4, sub = idx & 15;
+            const int vv = vg / nG, gg = vg - vv * nG;
+            const uint16_t* xg = src[vv] + (size_t)gg * 64 + 16 * (sub >> 2) + (sub & 3);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) raw[b] = __ldcg(xg + 4 * b);
+        }
+    };
+    uint16_t nraw[4] = {0, 0, 0, 0};
+    load((threadIdx.x - t0) & ~31, nraw);
     for (int base = ((threadIdx.x - t0) & ~31); base < total; base += nthreads) {
         const int idx = base + lane;
         const bool valid = idx < total;
         const int vg = idx >> 4, sub = idx & 15;
         const int w = sub >> 2, p = sub & 3;
         const int v = valid ? vg / nG : 0, g = valid ? vg - v * nG : 0;
+        uint16_t raw[4] = {nraw[0], nraw[1], nraw[2], nraw[3]};
+        if (base + nthreads < total) load(base + nthreads, nraw);
         float xv[4];
         float mx = 0.f, sum = 0.f;
         if (valid) {
-            const uint16_t* xg = src[v] + (size_t)g * 64 + 16 * w + p;
 #pragma unroll
-            for (int b = 0; b < 4; ++b) xv[b] = Half<DT>::to_f(__ldcg(xg + 4 * b));
+            for (int b = 0; b < 4; ++b) xv[b] = Half<DT>::to_f(raw[b]);
 #pragma unroll
             for (int b = 0; b < 4; ++b) {
                 mx = fmaxf(mx, fabsf(xv[b]));
@@ -247,6 +262,8 @@ struct DecShared {
     int nan_tok[8];
     const uint16_t* vec_ptr[16];
     int nunits, bad, nt_up, nt_dn, udn0, nudn, nseg, nlast, flag, abort, stopped;
+    int wpre[kDecMaxPairs + 1];  // prefix of the units' slice weights
+    int bnd[4];                  // this CTA's up and down slice bounds
     unsigned gen0;  // the grid barrier's generation before this call's round
     uint32_t tmem;
     alignas(8) uint64_t full[kDecMaxStages];
@@ -327,9 +344,24 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
     const bool stopped = S.stopped != 0;
     const int nG_up = a.H >> 6, nG_dn = a.I >> 6;
     const int gbytes = dec_b_group_bytes(N);
-    // ---- routing and plan, all threads (the producers need the plan first) ------
-    {
-        const int nthr = kDecThreadsAll;
+    // ---- the epilogue warps encode the tokens (the up phase's digit operand,
+    // ---- independent of the routing) while warps 0-7 route and plan
+    if (warp >= kWarpEpi0 && warp < kWarpMma0) {
+        const int te = tid - kTidEpi0;
+        for (int i = te; i < a.b_bytes / 16; i += kDecEpiThreads)
+            reinterpret_cast<uint4*>(s_B)[i] = make_uint4(0u, 0u, 0u, 0u);
+        if (te < a.M) S.vec_ptr[te] = a.x + (size_t)te * a.H;
+        bar_sync(kBarEpi, kDecEpiThreads);
+        if (!stopped) digitize_b<DT>(S.vec_ptr, a.M, a.H, N, T, GP, s_B, s_fs, kDecEpiThreads, kTidEpi0);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        bar_sync(kBarEpi, kDecEpiThreads);
+        if (te == 0) {
+            dstamp_thread(a, 3);
+            mbar_arrive(&S.b_ready[0]);
+        }
+    } else if (warp < kDecDeqWarps) {
+        // routing and plan by the first warpgroups (a named barrier over them)
+        constexpr int nthr = 32 * kDecDeqWarps;
         const int nlog = a.logits ? a.M * a.E : 0;
         for (int i = tid; i < nlog; i += nthr) {
             const float v = __ldcg(a.logits + i);
@@ -342,21 +374,59 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
                 S.scores[i] = __ldcg(a.scores_in + i);
             }
         }
-        __syncthreads();
+        bar_sync(kBarRoute, nthr);
         if (tid == 0) dstamp_thread(a, 22);
-        if (a.logits)
-            route_tokens(s_logits, S.nan_tok, a.M, a.E, a.K, 0, nthr, 0, S.inds, S.scores,
-                         a.trace ? a.trace + (size_t)blockIdx.x * kTracePointsDec + 25 : nullptr);
-        __syncthreads();
+        if (a.logits) {
+            if (a.M == 1) {  // one token: ranks over the warps
+                route_tokens(s_logits, S.nan_tok, a.M, a.E, a.K, 0, nthr, kBarRoute, S.inds, S.scores,
+                             a.trace ? a.trace + (size_t)blockIdx.x * kTracePointsDec + 25 : nullptr);
+            } else if (warp < a.M) {  // several: one warp per token replays the reduction tree
+                route_token_warp(s_logits + warp * a.E, a.E, a.K, S.inds + warp * a.K, S.scores + warp * a.K);
+            }
+        }
+        bar_sync(kBarRoute, nthr);
         if (tid == 0) dstamp_thread(a, 23);
-        if (warp == 0) plan_units_warp(S.inds, P, a.E, a.K, T, S.units, S.sorted, S.qinfo, &S.nunits, &S.bad);
-        __syncthreads();
+        if (warp == 0) {
+            plan_units_warp(S.inds, P, a.E, a.K, T, S.units, S.sorted, S.qinfo, &S.nunits, &S.bad);
+            __syncwarp();
+            // unit weights (c0 + tokens: the epilogue's work grows with them) and their prefix
+            const int U = S.nunits;
+            const int w0 = lane < U ? a.slice_c0 + __popc(S.units[lane].w) : 0;
+            const int w1 = lane + 32 < U ? a.slice_c0 + __popc(S.units[lane + 32].w) : 0;
+            int s0 = w0, s1 = w1;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t0 = __shfl_up_sync(0xffffffffu, s0, o), t1 = __shfl_up_sync(0xffffffffu, s1, o);
+                if (lane >= o) {
+                    s0 += t0;
+                    s1 += t1;
+                }
+            }
+            const int tot0 = __shfl_sync(0xffffffffu, s0, 31);
+            S.wpre[lane] = s0 - w0;
+            S.wpre[lane + 32] = tot0 + s1 - w1;
+            if (lane == 31) S.wpre[64] = tot0 + s1;
+        }
+        bar_sync(kBarRoute, nthr);
+        if (tid == 0) dstamp_thread(a, 24);
+        if (tid < 4) {
+            // CTA bx takes the 8-row granules of the (unit, row) space whose
+            // weight prefix falls in [W bx / G, W (bx + 1) / G)
+            const int U = S.nunits, G = gridDim.x;
+            const int rows = tid < 2 ? a.I : a.H, n = rows / 8;
+            const long long pos = (long long)n * S.wpre[U] * (blockIdx.x + (tid & 1)) / G;
+            int u = 0;
+            while (u < U && (long long)n * S.wpre[u + 1] < pos) ++u;
+            int b = U * rows;
+            if (u < U) {
+                const long long w = S.wpre[u + 1] - S.wpre[u], rem = pos - (long long)n * S.wpre[u];
+                b = (u * n + (int)((rem + w - 1) / w)) * 8;
+            }
+            S.bnd[tid] = b;
+        }
+        bar_sync(kBarRoute, nthr);
         if (tid == 0) {
-            dstamp_thread(a, 24);
-            const int U = S.nunits, G = gridDim.x, bx = blockIdx.x;
-            const long long n8u = (long long)U * a.I / 8, n8d = (long long)U * a.H / 8;
-            const int r0 = (int)(n8u * bx / G) * 8, r1 = (int)(n8u * (bx + 1) / G) * 8;
-            const int d0 = (int)(n8d * bx / G) * 8, d1 = (int)(n8d * (bx + 1) / G) * 8;
+            const int r0 = S.bnd[0], r1 = S.bnd[1], d0 = S.bnd[2], d1 = S.bnd[3];
             S.nt_up = make_tiles(r0, r1, a.I, 64, S.tiles_up, kDecMaxTiles);
             S.nt_dn = make_tiles(d0, d1, a.H, 128, S.tiles_dn, kDecMaxTiles);
             S.udn0 = d0 < d1 ? d0 / a.H : 0;
@@ -650,19 +720,6 @@ __global__ void __launch_bounds__(kDecThreadsAll, 1) moe_decode_kernel(const __g
         bool oke = true;
         long long w_d = 0, cy_epi = 0;
         const bool prof = a.trace != nullptr && te == 0;
-        {  // the up phase's digit operand: every token's x (vector v = token)
-            for (int i = te; i < a.b_bytes / 16; i += kDecEpiThreads)
-                reinterpret_cast<uint4*>(s_B)[i] = make_uint4(0u, 0u, 0u, 0u);
-            if (te < a.M) S.vec_ptr[te] = a.x + (size_t)te * a.H;
-            bar_sync(kBarEpi, kDecEpiThreads);
-            if (!stopped) digitize_b<DT>(S.vec_ptr, a.M, a.H, N, T, GP, s_B, s_fs, kDecEpiThreads, kTidEpi0);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            bar_sync(kBarEpi, kDecEpiThreads);
-            if (te == 0) {
-                dstamp_thread(a, 3);
-                mbar_arrive(&S.b_ready[0]);
-            }
-        }
         for (int ph = 0; ph < 2; ++ph) {
             const int nt = ph ? nt_dn : nt_up, nC = ph ? nC_dn : nC_up, nG = ph ? nG_dn : nG_up;
             const int4* tiles = ph ? S.tiles_dn : S.tiles_up;

@@ -46,9 +46,9 @@ constexpr int kDecCodeBytes = 128 * 128;   // a stage's codes: 128 rows x one 12
 constexpr int kDecSbBytes = 128 * 16;      // a stage's scales (and again biases): 128 rows x 16 B
 constexpr int kDecStageBytes = kDecCodeBytes + 2 * kDecSbBytes;  // 20 KB, a multiple of 1 KB
 constexpr int kDecMaxStages = 12;
-constexpr int kDecMaxTiles = 48;           // tiles per phase per CTA (host-checked bound)
+constexpr int kDecMaxTiles = 96;           // tiles per phase per CTA (host-checked bound)
 constexpr int kDecMaxPairs = 64;           // M * K
-constexpr int kDecMaxLastBlocks = 64;      // (unit, 64-row block) segments per CTA in the combine
+constexpr int kDecMaxLastBlocks = 128;     // (unit, 64-row block) segments per CTA in the combine
 constexpr int kDecAslots = 2;              // A slots per warpgroup (64 TMEM columns each)
 constexpr int kDecTmemCols = 512;
 constexpr int kTracePointsDec = 32;
@@ -81,6 +81,7 @@ struct DecodeArgs {
     int gs;
     int stages;              // ring stages (even)
     int spin_limit;          // polls of a bounded wait before it gives up
+    int slice_c0;            // CTA slices weigh a unit's rows c0 + its tokens (the epilogue's work)
     float clamp;
     // dynamic shared-memory carve-up (byte offsets from the 1024-aligned base)
     int off_ring, off_b, off_fs, off_red, off_logits;
