@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 OBJ = os.path.join(HERE, "_build")
 LIB_DIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIB_DIR, "libmomij_moe.so")
-SOURCES = ["route.cu", "gemv.cu", "layer.cu", "decode.cu", "block.cu", "prefill.cu", "ep.cu", "ep_host.cu", "misc.cu",
+SOURCES = ["route.cu", "gemv.cu", "layer.cu", "token.cu", "decode.cu", "block.cu", "prefill.cu", "ep.cu", "ep_host.cu", "misc.cu",
            "api.cu", "noalloc.cu"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

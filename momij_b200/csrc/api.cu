@@ -18,6 +18,7 @@
 #include "gemv_core.cuh"
 #include "decode.cuh"
 #include "layer.cuh"
+#include "token.cuh"
 #include "prefill.cuh"
 
 using namespace momij;
@@ -605,17 +606,169 @@ int run_layer_engine(const LayerCall& c, int dtype, int gs, const Workspace& ws,
     return cuda_status(e);
 }
 
-bool m1_on_tcgen05() {
-    const char* v = std::getenv("MOMIJ_DECODE_M1");
-    return v && std::strcmp(v, "tc") == 0;
+// ---- single-token streaming layer (token.cu) ---------------------------------
+using TokenFn = void (*)(const TokenArgs);
+
+// The up||gate codes [2E halves][I rows][H/4 bytes] seen as the 4D tensor
+// [128 B][I rows][H/512 column chunks][2E halves]: one box (128 B, 8 rows,
+// every chunk, 2 halves) is a tile of 8 up rows and the matching 8 gate rows,
+// laid out in shared memory as [half][chunk][row][128 B] (128-byte swizzle).
+// Cached per (device, address, shape).
+bool up_tile_map(const void* ptr, long long E, int I, int H, CUtensorMap* out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    const MapKey key{dev, ptr, E * 2 * I, H / 4, 8, 128, -I};  // negative half_rows: this 4D view
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+        *out = it->second;
+        return true;
+    }
+    auto enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t rb = (cuuint64_t)H / 4;
+    cuuint64_t gdim[4] = {128, (cuuint64_t)I, (cuuint64_t)H / 512, (cuuint64_t)(2 * E)};
+    cuuint64_t gstride[3] = {rb, 128, rb * (cuuint64_t)I};
+    cuuint32_t box[4] = {128, 8, (cuuint32_t)(H / 512), 2};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUtensorMap m;
+    if (enc(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(ptr), gdim, gstride, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    if (g_maps.size() >= 8192) g_maps.clear();
+    g_maps.emplace(key, m);
+    *out = m;
+    return true;
 }
 
-// The fused layer: one token on the warp-level engine, 2..8 tokens on the
-// tcgen05 kernel; kNotApplicable lets the caller fall back to the
-// multi-kernel path.
+// One token's whole layer as one cooperative kernel that streams the expert
+// weights by TMA (token.cu); kNotApplicable when the shapes, the alignment or
+// the shared memory do not fit (gs 64, K <= 8, H <= 4096, H and I multiples
+// of 512, E <= 512 when routing from logits).
+int run_token_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, cudaStream_t st) {
+    if (c.M != 1 || gs != 64 || c.K > kTokMaxK || c.K < 1 || (c.logits && c.E > kTokMaxE) || c.H % 512 ||
+        c.I % 512 || c.H > 4096)
+        return kNotApplicable;
+    if (!aligned(c.w_ug, 16) || !aligned(c.w_dn, 16) || !aligned(c.s_ug, 16) || !aligned(c.b_ug, 16) ||
+        !aligned(c.s_dn, 16) || !aligned(c.b_dn, 16) || !aligned(c.x, 16) || !aligned(ws.act, 16))
+        return kNotApplicable;
+    const int G = current_device_sm_count();
+    if (G <= 0) return kNotApplicable;
+    const long long T = (long long)c.K * c.I / 8;
+    const int max_tiles = (int)((T + G - 1) / G);
+    const int rpc = (c.H + G - 1) / G;
+    if (max_tiles > kTokMaxTiles || rpc > kTokDnRows) return kNotApplicable;
+    TokenArgs a{};
+    const long long E = c.E;
+    const int srb_up = c.H / 32, srb_dn = c.I / 32;  // scale bytes per row (gs 64)
+    if (!up_tile_map(c.w_ug, E, c.I, c.H, &a.map[0]) ||
+        !weight_map(c.s_ug, E * 2 * c.I, srb_up, srb_up, 8, c.I, &a.map[1]) ||
+        !weight_map(c.b_ug, E * 2 * c.I, srb_up, srb_up, 8, c.I, &a.map[2]) ||
+        !weight_map(c.w_dn, E * c.H, c.I / 4, 128, rpc, 0, &a.map[3]) ||
+        !weight_map(c.s_dn, E * c.H, srb_dn, 16, rpc, 0, &a.map[4]) ||
+        !weight_map(c.b_dn, E * c.H, srb_dn, 16, rpc, 0, &a.map[5]))
+        return kNotApplicable;
+    a.logits = c.logits;
+    a.inds_in = c.inds_in;
+    a.scores_in = c.scores_in;
+    a.inds_out = c.inds_out;
+    a.scores_out = c.scores_out;
+    a.x = static_cast<const uint16_t*>(c.x);
+    a.act = ws.act;
+    a.y = c.resid_h ? nullptr : static_cast<uint16_t*>(c.y);
+    a.h = static_cast<uint16_t*>(c.resid_h);
+    a.ctrl = ws.plan;
+    a.bar64 = reinterpret_cast<unsigned long long*>(ws.plan + kCtrlBar64);
+    a.stop = g_stop_flag.load();
+    a.H = c.H;
+    a.I = c.I;
+    a.E = c.E;
+    a.K = c.K;
+    a.spin_limit = spin_limit();
+    a.rows_per_cta = rpc;
+    a.clamp = c.clamp;
+    // shared memory (from a 1024-aligned base): the stage ring, the logits,
+    // then one region that the up phase (x digits, their group factors, up
+    // partials) and the down phase (act digits, factors, down partials) use in turn
+    size_t off = 0;
+    a.off_ring = (int)off;
+    off += (size_t)kTokStages * kTokStageBytes;
+    a.off_logits = (int)off;
+    off = align_up(off + 4 * (size_t)kTokThreads, 128);
+    const size_t reg = off;
+    a.off_xb = (int)off;
+    off = align_up(off + tok_b_bytes(c.H), 16);
+    a.off_xfs = (int)off;
+    off = align_up(off + 8 * (size_t)(c.H / 64), 16);
+    a.off_red_up = (int)off;
+    off += 4 * (size_t)max_tiles * 16 * tok_red_stride(c.H / 512);
+    const size_t end_up = off;
+    off = reg;
+    a.off_ab = (int)off;
+    off = align_up(off + (size_t)c.K * tok_b_bytes(c.I), 16);
+    a.off_afs = (int)off;
+    off = align_up(off + 8 * (size_t)c.K * (c.I / 64), 16);
+    a.off_red_dn = (int)off;
+    off += 4 * (size_t)c.K * kTokDnRows * tok_red_stride(c.I / 512);
+    off = std::max(off, end_up) + 1024;  // + the alignment slack of the base
+    if (off > (size_t)max_dyn_smem()) return kNotApplicable;
+    TokenFn fn = dtype == MOMIJ_DTYPE_BF16 ? moe_token_kernel<MOMIJ_DTYPE_BF16> : moe_token_kernel<MOMIJ_DTYPE_F16>;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)off) != cudaSuccess)
+        return MOMIJ_ERR_CUDA;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kTokThreads, off) != cudaSuccess || per_sm < 1)
+        return kNotApplicable;
+    a.trace = next_trace_slot(G);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(kTokThreads);
+    cfg.dynamicSmemBytes = off;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    static bool pdl_with_coop = true;  // dropped if the driver refuses the pair
+    cfg.numAttrs = (pdl_enabled() && pdl_with_coop) ? 2 : 1;
+    const int slot = prof_begin(MOMIJ_KERNEL_LAYER, st);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, fn, a);
+    if (e != cudaSuccess && cfg.numAttrs == 2) {
+        cudaGetLastError();
+        pdl_with_coop = false;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, fn, a);
+    }
+    prof_end(slot, st);
+    return cuda_status(e);
+}
+
+// Engine of single-token layers: MOMIJ_DECODE_M1=warp selects the warp-level
+// engine (layer.cu), =tc the tcgen05 kernel (decode.cu); the default is the
+// TMA-streaming kernel (token.cu), with the warp-level engine for the shapes
+// it does not take.
+int m1_engine() {
+    static const int v = [] {
+        const char* e = std::getenv("MOMIJ_DECODE_M1");
+        if (e && std::strcmp(e, "tc") == 0) return 2;
+        if (e && std::strcmp(e, "warp") == 0) return 1;
+        return 0;
+    }();
+    return v;
+}
+
+// The fused layer: one token on the streaming kernel (or the engine the
+// environment selects), 2..8 tokens on the tcgen05 kernel; kNotApplicable
+// lets the caller fall back to the multi-kernel path.
 int run_fused_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, cudaStream_t st) {
     if (!fused_enabled()) return kNotApplicable;
-    if (c.M == 1 && !m1_on_tcgen05()) {
+    if (c.M == 1 && m1_engine() == 0) {
+        const int rc = run_token_layer(c, dtype, gs, ws, st);
+        if (rc != kNotApplicable) return rc;
+    }
+    if (c.M == 1 && m1_engine() != 2) {
         const int rc = run_layer_engine(c, dtype, gs, ws, st);
         if (rc != kNotApplicable) return rc;
     }

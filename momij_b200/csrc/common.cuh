@@ -13,7 +13,7 @@ constexpr int kChunk = 256;          // codes of one row a warp handles per tile
 constexpr int kDigitGroup = 64;      // x elements sharing one digit exponent
 constexpr int kDgStride = 200;       // bytes per digit group: three 64-B int8 planes + 8 B pad (bank spread)
 constexpr int kMaxTmax = 8;          // max pairs (token columns) per unit
-constexpr int kPlanHeader = 4;       // [0]=units, [1]=status, [2..3] reserved
+constexpr int kPlanHeader = 8;       // [0]=units, [1]=status, then the fused kernels' control words (decode.cuh)
 
 // ---- 16-bit float formats --------------------------------------------------
 template <int DT>

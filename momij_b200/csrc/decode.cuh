@@ -11,8 +11,9 @@ namespace momij {
 
 // Control words at the start of the workspace (the work-plan header of the
 // multi-kernel path): [1] routing status, [2] sticky error word (a bounded
-// wait that gave up), [3] grid-barrier arrivals, [4] grid-barrier generation.
-constexpr int kCtrlStatus = 1, kCtrlError = 2, kCtrlArrive = 3, kCtrlGen = 4;
+// wait that gave up), [3] grid-barrier arrivals, [4] grid-barrier generation,
+// [6..7] the single-token kernel's 64-bit grid-barrier arrival count.
+constexpr int kCtrlStatus = 1, kCtrlError = 2, kCtrlArrive = 3, kCtrlGen = 4, kCtrlBar64 = 6;
 
 // Warp roles of the decode kernel (20 warps):
 //   0-7   dequantise: warpgroup d (warps 4d..4d+3) turns the 16-code words of

@@ -31,7 +31,7 @@ namespace {
 // Bytes of a work plan for MOMIJ_NOALLOC_MAX_PAIRS pairs: header + 4 ints per
 // unit + 1 int per pair, rounded up to 256 (the layout the plan kernel writes).
 constexpr size_t kNoAllocPlanBytes =
-    ((sizeof(int32_t) * (4 + 5 * (size_t)MOMIJ_NOALLOC_MAX_PAIRS) + 255) / 256) * 256;
+    ((sizeof(int32_t) * (momij::kPlanHeader + 5 * (size_t)MOMIJ_NOALLOC_MAX_PAIRS) + 255) / 256) * 256;
 
 static __device__ __align__(256) int32_t g_noalloc_plan[kNoAllocPlanBytes / sizeof(int32_t)];
 

@@ -32,7 +32,7 @@ def test_workspace_size_grows_with_pairs():
     a = moe.workspace_size(1, 8, 4096, 1536)
     b = moe.workspace_size(8, 8, 4096, 1536)
     assert 0 < a < b
-    # plan (header + 5 ints per pair) + act + down + inds + scores + one
+    # plan (8-int header + 5 ints per pair) + act + down + inds + scores + one
     # completion counter per 64 output rows + the grouped path's tables
     # (offsets for up to 1024 experts, pair ids, weights, status words, block
     # list of up to P/128 + 1025 blocks) + its exact-recomputation list (a
@@ -41,7 +41,7 @@ def test_workspace_size_grows_with_pairs():
     up = lambda n: -(-n // 256) * 256
     grp = 4 * (1025 + 2 * P + 4 + 4 + 4 * (P // 128 + 1024 + 1))
     fix = 16 + 16 * -(-P * I // 8)
-    expect = (up(4 * (4 + 5 * P)) + P * I * 2 + P * 4096 * 2 + 256 + 256 + 256 + up(grp) + up(fix))
+    expect = (up(4 * (8 + 5 * P)) + P * I * 2 + P * 4096 * 2 + 256 + 256 + 256 + up(grp) + up(fix))
     assert a == expect
     assert moe.workspace_size(-1, 8, 16, 16) == 0
 
