@@ -18,9 +18,9 @@
 //      partial sums go to shared memory and each row pair then gets its
 //      staged clamped SwiGLU -> act[slot, I];
 //   3. grid barrier (act complete; the down weights are already streaming);
-//   4. down phase: warps 2k and 2k + 1 encode act[k] and take its two 16-row
-//      halves; one stage = one 128-byte code column of the CTA's rows for
-//      every expert slot;
+//   4. down phase: the CTA encodes the K act vectors, then warps 2k and
+//      2k + 1 take expert slot k's two 16-row halves; one stage = one
+//      128-byte code column of the CTA's rows for every expert slot;
 //   5. the CTA combines its own rows: y[n] = cast(sum_k float(down_k[n]) *
 //      score_k) in k order (MapleMoE.swift:76-78), or h[n] = cast(h[n] +
 //      cast(acc)) (maple_score_resid) -- no staging of the down outputs and no
@@ -57,102 +57,126 @@ __device__ __forceinline__ void tstamp(const TokenArgs& a, int i) {
     }
 }
 
-// Loads the 16 elements of encoder task `task` (vector v at src + v * Kd,
-// group (task >> 2) % (Kd / 64), elements 16 (task & 3) .. + 15); bypasses L1
-// (the vectors may have been written by other CTAs).
-__device__ __forceinline__ void tok_load_task(const uint16_t* __restrict__ src, int Kd, int task, uint4 (&raw)[2]) {
-    const int nG = Kd >> 6, vg = task >> 2, v = vg / nG;
-    const uint4* sp = reinterpret_cast<const uint4*>(src + (size_t)v * Kd + (vg - v * nG) * 64 + 16 * (task & 3));
-    raw[0] = __ldcg(sp);
-    raw[1] = __ldcg(sp + 1);
+// Encoder tasks: EPT (8 or 16) consecutive elements of one 64-element group
+// (vector v at src + v * Kd, Kd a multiple of 512); task = (v * nG + G) *
+// (64 / EPT) + u, u the task's part of its group.
+template <int EPT>
+struct EncTask {
+    static constexpr int kWords = EPT / 2;  // 16-bit elements in 32-bit words
+    uint32_t w[kWords];
+};
+
+// Loads one task's elements; bypasses L1 (the vectors may have been written
+// by other CTAs).
+template <int EPT>
+__device__ __forceinline__ void tok_load_task(const uint16_t* __restrict__ src, int Kd, int task, EncTask<EPT>& r) {
+    const uint4* sp = reinterpret_cast<const uint4*>(src + (size_t)task * EPT);  // tasks tile the vectors in order
+#pragma unroll
+    for (int i = 0; i < EPT / 8; ++i) {
+        const uint4 v = __ldcg(sp + i);
+        r.w[4 * i] = v.x;
+        r.w[4 * i + 1] = v.y;
+        r.w[4 * i + 2] = v.z;
+        r.w[4 * i + 3] = v.w;
+    }
 }
 
-// Encodes one task's 16 elements into the digit operand.  The four tasks of
-// a 64-element group sit in four consecutive lanes (all 32 lanes call it;
-// `valid` false only takes part in the shuffles).  Layout, per vector and
-// 512-element code column c (2 KB): [slab s (4)][class pair (2)][active B
-// lane L (16)][16 B], lane L's 16 bytes the fragments (b0, b1) of the pair's
-// even then odd class.  Group j of the column (G = 8c + j) feeds slab j & 3
-// through A lanes with t >> 1 = j >> 2; its in-group byte bb goes to A lane
-// t & 1 = bb >> 3, register (bb >> 2) & 1, byte bb & 3, and its digit d to
-// B lane L = 8 (j >> 2) + 4 (bb >> 3) + d.  fs[v * nG + G] = (2^(E-27), sum
-// of the group), the sum in the order of the tcgen05 decode kernel's encoder.
-// Digits: y = 2^24 d0 + 2^16 d1 + 2^8 d2 + d3 with d1..d3 in [-128, 127]; the
-// bytes of (y + 0x808080) ^ 0x808080 are d3, d2, d1, d0 (each digit's byte
-// is its carry-free remainder), and a 4 x 4 byte transpose gathers digit dd
-// of the four class-p elements into one word.
-template <int DT>
-__device__ __forceinline__ void tok_encode(const uint4 (&raw)[2], bool valid, int task, int Kd,
+// Encodes one task into the digit operand.  The 64 / EPT tasks of a group sit
+// in consecutive lanes (all 32 lanes call it; `valid` false only takes part
+// in the shuffles).  Layout, per vector and 512-element code column c (2 KB):
+// [slab s (4)][class pair (2)][active B lane L (16)][16 B], lane L's 16 bytes
+// the fragments (b0, b1) of the pair's even then odd class.  Group j of the
+// column (G = 8c + j) feeds slab j & 3 through A lanes with t >> 1 = j >> 2;
+// its in-group byte bb goes to A lane t & 1 = bb >> 3, register (bb >> 2) &
+// 1, byte bb & 3, and its digit d to B lane L = 8 (j >> 2) + 4 (bb >> 3) + d.
+// fs[v * nG + G] = (2^(E-27), sum of the group).  Digits: y = 2^24 d0 +
+// 2^16 d1 + 2^8 d2 + d3 with d1..d3 in [-128, 127]; the bytes of (y +
+// 0x808080) ^ 0x808080 are d3, d2, d1, d0 (each digit's byte is its
+// carry-free remainder), and byte permutes gather digit dd of the task's
+// class-p elements into one store.
+template <int DT, int EPT>
+__device__ __forceinline__ void tok_encode(const EncTask<EPT>& r, bool valid, int task, int Kd,
                                            unsigned char* __restrict__ B, float2* __restrict__ fs) {
-    const int nG = Kd >> 6, vg = task >> 2, v = vg / nG, G = vg - v * nG, u = task & 3;
-    const uint32_t w[8] = {raw[0].x, raw[0].y, raw[0].z, raw[0].w, raw[1].x, raw[1].y, raw[1].z, raw[1].w};
-    float xv[16];
+    constexpr int TPG = 64 / EPT, NB = EPT / 4;  // tasks per group, code bytes per task
+    float xv[EPT];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        xv[2 * i] = Half<DT>::to_f(static_cast<uint16_t>(w[i] & 0xffffu));
-        xv[2 * i + 1] = Half<DT>::to_f(static_cast<uint16_t>(w[i] >> 16));
+    for (int i = 0; i < EPT / 2; ++i) {
+        xv[2 * i] = Half<DT>::to_f(static_cast<uint16_t>(r.w[i] & 0xffffu));
+        xv[2 * i + 1] = Half<DT>::to_f(static_cast<uint16_t>(r.w[i] >> 16));
     }
-    float mx = 0.f, sp4[4];
+    float mx = 0.f, sp[4];
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-        sp4[p] = ((xv[p] + xv[4 + p]) + xv[8 + p]) + xv[12 + p];
+        sp[p] = xv[p];
 #pragma unroll
-        for (int b = 0; b < 4; ++b) mx = fmaxf(mx, fabsf(xv[4 * b + p]));
+        for (int b = 1; b < NB; ++b) sp[p] += xv[4 * b + p];
+#pragma unroll
+        for (int b = 0; b < NB; ++b) mx = fmaxf(mx, fabsf(xv[4 * b + p]));
     }
-    float W = (sp4[0] + sp4[1]) + (sp4[2] + sp4[3]);
+    float W = (sp[0] + sp[1]) + (sp[2] + sp[3]);
 #pragma unroll
-    for (int o = 1; o < 4; o <<= 1) {
+    for (int o = 1; o < TPG; o <<= 1) {
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         W += __shfl_xor_sync(0xffffffffu, W, o);
     }
     if (!valid) return;
-    int E = (mx > 0.f) ? ilogbf(mx) : 0;
+    const int fe = (__float_as_int(mx) >> 23) & 0xff;
+    int E = fe ? fe - 127 : (mx > 0.f ? ilogbf(mx) : 0);
     E = max(E, -100);
-    const float scale = ldexpf(1.f, 21 - E);
-    const int j = G & 7;
+    const float scale = __int_as_float((148 - E) << 23);  // 2^(21 - E)
+    const int vg = task / TPG, u = task - vg * TPG;
+    const int nG = Kd >> 6, v = vg / nG, G = vg - v * nG, j = G & 7;
+    const int bb0 = u * NB;  // first in-group byte of the task
     unsigned char* gb = B + (size_t)v * tok_b_bytes(Kd) + (G >> 3) * 2048 + (j & 3) * 512 +
-                        ((j >> 2) * 8 + (u >> 1) * 4) * 16 + (u & 1) * 4;
+                        ((j >> 2) * 8 + (bb0 >> 3) * 4) * 16 + ((bb0 >> 2) & 1) * 4 + (bb0 & 3);
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-        uint32_t e[4];
+        uint32_t e[NB];
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
+        for (int b = 0; b < NB; ++b) {
             const int y = __float2int_rn(xv[4 * b + p] * scale) * (1 << (2 * (3 - p)));
             e[b] = (uint32_t)(y + 0x808080) ^ 0x808080u;
         }
-        const uint32_t t0 = __byte_perm(e[0], e[1], 0x5140), t1 = __byte_perm(e[2], e[3], 0x5140);
-        const uint32_t t2 = __byte_perm(e[0], e[1], 0x7362), t3 = __byte_perm(e[2], e[3], 0x7362);
         unsigned char* gp = gb + (p >> 1) * 256 + (p & 1) * 8;
-        *reinterpret_cast<uint32_t*>(gp + 3 * 16) = __byte_perm(t0, t1, 0x5410);  // d3 (256^0)
-        *reinterpret_cast<uint32_t*>(gp + 2 * 16) = __byte_perm(t0, t1, 0x7632);  // d2
-        *reinterpret_cast<uint32_t*>(gp + 1 * 16) = __byte_perm(t2, t3, 0x5410);  // d1
-        *reinterpret_cast<uint32_t*>(gp + 0 * 16) = __byte_perm(t2, t3, 0x7632);  // d0 (256^3)
+        if (NB == 4) {
+            const uint32_t t0 = __byte_perm(e[0], e[1], 0x5140), t1 = __byte_perm(e[2 % NB], e[3 % NB], 0x5140);
+            const uint32_t t2 = __byte_perm(e[0], e[1], 0x7362), t3 = __byte_perm(e[2 % NB], e[3 % NB], 0x7362);
+            *reinterpret_cast<uint32_t*>(gp + 3 * 16) = __byte_perm(t0, t1, 0x5410);  // d3 (256^0)
+            *reinterpret_cast<uint32_t*>(gp + 2 * 16) = __byte_perm(t0, t1, 0x7632);  // d2
+            *reinterpret_cast<uint32_t*>(gp + 1 * 16) = __byte_perm(t2, t3, 0x5410);  // d1
+            *reinterpret_cast<uint32_t*>(gp + 0 * 16) = __byte_perm(t2, t3, 0x7632);  // d0 (256^3)
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)  // digit 3 - i: byte i of both elements
+                *reinterpret_cast<uint16_t*>(gp + (3 - i) * 16) =
+                    static_cast<uint16_t>(__byte_perm(e[0], e[1 % NB], i | ((4 + i) << 4)));
+        }
     }
-    if (u == 0) fs[v * nG + G] = make_float2(ldexpf(1.f, E - 27), W);
+    if (u == 0)
+        fs[v * nG + G] = make_float2(E > -100 ? __int_as_float((E + 100) << 23) : ldexpf(1.f, E - 27), W);
 }
 
 // Encodes vectors [v0, v0 + nvec) of src (row length Kd) by `nthr` threads
-// (whole warps, thread index `tt` from 0), each loading all its tasks before
-// it computes.
-template <int DT>
+// (whole warps, thread index `tt` from 0), EPT elements per task, each thread
+// loading all its tasks of a pass before it computes.
+template <int DT, int EPT>
 __device__ void tok_digitize(const uint16_t* __restrict__ src, int v0, int nvec, int Kd, unsigned char* __restrict__ B,
                              float2* __restrict__ fs, int tt, int nthr) {
-    constexpr int NT = 2;
-    const int total = nvec * (Kd >> 6) * 4, first = v0 * (Kd >> 6) * 4;
+    constexpr int NT = 3;
+    const int total = nvec * Kd / EPT, first = v0 * Kd / EPT;
     const int lane = tt & 31;
     for (int base0 = tt & ~31; base0 < total; base0 += NT * nthr) {
-        uint4 raw[NT][2];
+        EncTask<EPT> raw[NT];
 #pragma unroll
         for (int q = 0; q < NT; ++q) {
-            raw[q][0] = raw[q][1] = make_uint4(0u, 0u, 0u, 0u);
             const int task = base0 + q * nthr + lane;
-            if (task < total) tok_load_task(src, Kd, first + task, raw[q]);
+            if (task < total) tok_load_task<EPT>(src, Kd, first + task, raw[q]);
         }
 #pragma unroll
         for (int q = 0; q < NT; ++q) {
             const int base = base0 + q * nthr;
             if (base >= total) break;  // warp-uniform
-            tok_encode<DT>(raw[q], base + lane < total, first + min(base + lane, total - 1), Kd, B, fs);
+            tok_encode<DT, EPT>(raw[q], base + lane < total, first + min(base + lane, total - 1), Kd, B, fs);
         }
     }
 }
@@ -232,9 +256,9 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
     tstamp(a, 1);
 
     // ---- 1. routing first (it gates the weight stream), the token's loads in flight
-    const int xtasks = (H >> 6) * 4;  // <= kTokThreads (H <= 4096)
-    uint4 xraw[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
-    if (tid < xtasks) tok_load_task(a.x, H, tid, xraw);
+    const int xtasks = H / 8;  // 8-element encoder tasks of the token (<= kTokCompute: H <= 4096)
+    EncTask<8> xraw;
+    if (tid < xtasks) tok_load_task<8>(a.x, H, tid, xraw);
     if (tid == 0) s_stop = a.stop ? __ldcg(a.stop) : 0;
     const float lc = (a.logits && tid < E) ? __ldcg(a.logits + tid) : -INFINITY;
     int flag;  // a NaN logit (routing from logits) or an expert index out of range (given indices)
@@ -342,26 +366,16 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kTokRegsCompute));
 
     // ---- token encoding and scores while the first stages land -----------------------
-    if (tid < ((xtasks + 31) & ~31)) tok_encode<DT>(xraw, tid < xtasks, min(tid, xtasks - 1), H, s_xb, s_xfs);
+    if (tid < ((xtasks + 31) & ~31)) tok_encode<DT, 8>(xraw, tid < xtasks, min(tid, xtasks - 1), H, s_xb, s_xfs);
     if (a.logits && !flag) {
-        // softmax denominator over all experts (max = the top-ranked logit)
+        // softmax denominator over all experts (max = the top-ranked logit);
+        // the renormalised scores follow after the up||gate phase
         float ez = tid < E ? expf(lc - s_max) : 0.f;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ez += __shfl_xor_sync(0xffffffffu, ez, o);
         if (lane == 0) s_part[warp] = ez;
-    } else if (a.logits && tid < 32) {
-        route_scores_warp(s_logits, E, K, s_inds, s_scores);
     }
     bar_sync(1, kTokCompute);
-    if (a.logits && !flag && tid < 32) {
-        // the selected gates renormalised by their sum in k order
-        float z = 0.f;
-        for (int w = 0; w < kTokWarps; ++w) z += s_part[w];
-        const float gate = lane < K ? expf(s_logits[s_inds[lane]] - s_max) / z : 0.f;
-        float sum = 0.f;
-        for (int k = 0; k < K; ++k) sum += __shfl_sync(0xffffffffu, gate, k);
-        if (lane < K) s_scores[lane] = gate / sum;
-    }
     tstamp(a, 3);
 
     // Digit operand fragments of a code column (bf[slab][class] = (b0, b1);
@@ -474,15 +488,28 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
         }
         a.act[(size_t)k * I + i0 + i] = swiglu_staged<DT>(up, gate, a.clamp);
     }
-    if (bx == 0 && tid < K) {
-        if (a.inds_out) a.inds_out[tid] = s_inds[tid];
-        if (a.scores_out) a.scores_out[tid] = s_scores[tid];
+    if (a.logits && warp == kTokWarps - 1) {
+        if (!flag) {
+            // the selected gates renormalised by their sum in k order
+            float z = 0.f;
+            for (int w = 0; w < kTokWarps; ++w) z += s_part[w];
+            const float gate = lane < K ? expf(s_logits[s_inds[lane]] - s_max) / z : 0.f;
+            float sum = 0.f;
+            for (int k = 0; k < K; ++k) sum += __shfl_sync(0xffffffffu, gate, k);
+            if (lane < K) s_scores[lane] = gate / sum;
+        } else {
+            route_scores_warp(s_logits, E, K, s_inds, s_scores);
+        }
     }
     // the residual rows this CTA updates at the end, in flight meanwhile
     const uint16_t hres = (a.h && tid < nrows) ? a.h[n0 + tid] : (uint16_t)0;
 
     // ---- 3. grid barrier ------------------------------------------------------------
     bar_sync(1, kTokCompute);
+    if (bx == 0 && tid < K) {
+        if (a.inds_out) a.inds_out[tid] = s_inds[tid];
+        if (a.scores_out) a.scores_out[tid] = s_scores[tid];
+    }
     tstamp(a, 5);
     if (tid == 0) {
         const bool okb = tok_grid_barrier(a.bar64, a.spin_limit);
@@ -493,15 +520,14 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
     const bool fine = s_flag != 0 && !s_abort;
     tstamp(a, 6);
 
-    // ---- 4. down phase: warps 2k, 2k + 1 encode act[k], then take its two 16-row halves
+    // ---- 4. down phase: the K act vectors encoded, then warp 2k + q takes
+    // expert slot k's 16-row half q
+    if (fine && nrows > 0) tok_digitize<DT, 16>(a.act, 0, K, I, s_ab, s_afs, tid, kTokCompute);
+    bar_sync(1, kTokCompute);
     if (nrows > 0) {
         const int k = warp >> 1, q = warp & 1;
         const int row = g + 8 * (t & 1);
         const bool mine = k < K && 16 * q < nrows;
-        if (fine && k < K) {
-            tok_digitize<DT>(a.act, k, 1, I, s_ab, s_afs, tid & 63, 64);
-            bar_sync(2 + k, 64);
-        }
         okw = true;
 #pragma unroll 1
         for (int c = 0; c < ncol_dn; ++c) {

@@ -10,7 +10,7 @@ constexpr int kTokCompute = 32 * kTokWarps;
 constexpr int kTokThreads = kTokCompute + 128;      // + the producer warpgroup (one lane issues the TMA loads)
 // Registers per thread: at launch (the launch-bounds maximum for 640 threads),
 // then moved from the producer warpgroup to the compute warps by setmaxnreg.
-constexpr int kTokRegsLaunch = 96, kTokRegsCompute = 112, kTokRegsProducer = 24;
+constexpr int kTokRegsLaunch = 96, kTokRegsCompute = 112, kTokRegsProducer = 32;
 static_assert(kTokCompute * kTokRegsCompute + 128 * kTokRegsProducer <= kTokThreads * kTokRegsLaunch,
               "register split exceeds the launch's registers");
 constexpr int kTokStages = 4;                       // ring stages
