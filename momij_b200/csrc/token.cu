@@ -93,7 +93,11 @@ __device__ __forceinline__ void tok_load_task(const uint16_t* __restrict__ src, 
 // 2^16 d1 + 2^8 d2 + d3 with d1..d3 in [-128, 127]; the bytes of (y +
 // 0x808080) ^ 0x808080 are d3, d2, d1, d0 (each digit's byte is its
 // carry-free remainder), and byte permutes gather digit dd of the task's
-// class-p elements into one store.
+// class-p elements into one store.  Rounding: x * 2^(21-E) + 1.5 * 2^23 is
+// rint(x * 2^(21-E)) + 1.5 * 2^23 exactly (|x * 2^(21-E)| < 2^22), so the
+// integer bits of that sum, times 4^(3-p), plus the digit offset are one
+// integer multiply-add: y + 0x808080 = bits * 4^(3-p) + (0x808080 -
+// 0x4B400000 * 4^(3-p)) modulo 2^32.
 template <int DT, int EPT>
 __device__ __forceinline__ void tok_encode(const EncTask<EPT>& r, bool valid, int task, int Kd,
                                            unsigned char* __restrict__ B, float2* __restrict__ fs) {
@@ -131,11 +135,13 @@ __device__ __forceinline__ void tok_encode(const EncTask<EPT>& r, bool valid, in
                         ((j >> 2) * 8 + (bb0 >> 3) * 4) * 16 + ((bb0 >> 2) & 1) * 4 + (bb0 & 3);
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
+        constexpr uint32_t kMagic = 0x4B400000u;  // bits of 1.5 * 2^23
+        const uint32_t mul = 1u << (2 * (3 - p)), add = 0x808080u - kMagic * mul;
         uint32_t e[NB];
 #pragma unroll
         for (int b = 0; b < NB; ++b) {
-            const int y = __float2int_rn(xv[4 * b + p] * scale) * (1 << (2 * (3 - p)));
-            e[b] = (uint32_t)(y + 0x808080) ^ 0x808080u;
+            const uint32_t bits = __float_as_uint(fmaf(xv[4 * b + p], scale, 12582912.f));
+            e[b] = (bits * mul + add) ^ 0x808080u;
         }
         unsigned char* gp = gb + (p >> 1) * 256 + (p & 1) * 8;
         if (NB == 4) {
