@@ -85,7 +85,11 @@ __device__ __forceinline__ void tok_load_task(const uint16_t* __restrict__ src, 
 // in consecutive lanes (all 32 lanes call it; `valid` false only takes part
 // in the shuffles).  Layout, per vector and 512-element code column c (2 KB):
 // [slab s (4)][class pair (2)][active B lane L (16)][16 B], lane L's 16 bytes
-// the fragments (b0, b1) of the pair's even then odd class.  Group j of the
+// the fragments (b0, b1) of the pair's even then odd class, stored at entry
+// (L & 8) | ((L & 7) ^ s) with the two 8-byte halves swapped when L >= 8 --
+// so that the encoder's stores of a warp (its groups differ in slab and row)
+// fall into distinct banks, while a reader's 16 lanes still cover one
+// contiguous 256-byte block.  Group j of the
 // column (G = 8c + j) feeds slab j & 3 through A lanes with t >> 1 = j >> 2;
 // its in-group byte bb goes to A lane t & 1 = bb >> 3, register (bb >> 2) &
 // 1, byte bb & 3, and its digit d to B lane L = 8 (j >> 2) + 4 (bb >> 3) + d.
@@ -131,8 +135,10 @@ __device__ __forceinline__ void tok_encode(const EncTask<EPT>& r, bool valid, in
     const int vg = task / TPG, u = task - vg * TPG;
     const int nG = Kd >> 6, v = vg / nG, G = vg - v * nG, j = G & 7;
     const int bb0 = u * NB;  // first in-group byte of the task
-    unsigned char* gb = B + (size_t)v * tok_b_bytes(Kd) + (G >> 3) * 2048 + (j & 3) * 512 +
-                        ((j >> 2) * 8 + (bb0 >> 3) * 4) * 16 + ((bb0 >> 2) & 1) * 4 + (bb0 & 3);
+    const int sl = j & 3, hi = j >> 2;  // slab, row of the entries (L >> 3)
+    unsigned char* gb = B + (size_t)v * tok_b_bytes(Kd) + (G >> 3) * 2048 + sl * 512 + hi * 128 +
+                        ((bb0 >> 2) & 1) * 4 + (bb0 & 3);
+    const int ent0 = (bb0 >> 3) * 4;  // entry of digit 0 within the row, before the swizzle
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
         constexpr uint32_t kMagic = 0x4B400000u;  // bits of 1.5 * 2^23
@@ -143,18 +149,19 @@ __device__ __forceinline__ void tok_encode(const EncTask<EPT>& r, bool valid, in
             const uint32_t bits = __float_as_uint(fmaf(xv[4 * b + p], scale, 12582912.f));
             e[b] = (bits * mul + add) ^ 0x808080u;
         }
-        unsigned char* gp = gb + (p >> 1) * 256 + (p & 1) * 8;
+        unsigned char* gp = gb + (p >> 1) * 256 + (((p & 1) ^ hi) * 8);
+        auto ent = [&](int d) { return ((ent0 + d) ^ sl) * 16; };
         if (NB == 4) {
             const uint32_t t0 = __byte_perm(e[0], e[1], 0x5140), t1 = __byte_perm(e[2 % NB], e[3 % NB], 0x5140);
             const uint32_t t2 = __byte_perm(e[0], e[1], 0x7362), t3 = __byte_perm(e[2 % NB], e[3 % NB], 0x7362);
-            *reinterpret_cast<uint32_t*>(gp + 3 * 16) = __byte_perm(t0, t1, 0x5410);  // d3 (256^0)
-            *reinterpret_cast<uint32_t*>(gp + 2 * 16) = __byte_perm(t0, t1, 0x7632);  // d2
-            *reinterpret_cast<uint32_t*>(gp + 1 * 16) = __byte_perm(t2, t3, 0x5410);  // d1
-            *reinterpret_cast<uint32_t*>(gp + 0 * 16) = __byte_perm(t2, t3, 0x7632);  // d0 (256^3)
+            *reinterpret_cast<uint32_t*>(gp + ent(3)) = __byte_perm(t0, t1, 0x5410);  // d3 (256^0)
+            *reinterpret_cast<uint32_t*>(gp + ent(2)) = __byte_perm(t0, t1, 0x7632);  // d2
+            *reinterpret_cast<uint32_t*>(gp + ent(1)) = __byte_perm(t2, t3, 0x5410);  // d1
+            *reinterpret_cast<uint32_t*>(gp + ent(0)) = __byte_perm(t2, t3, 0x7632);  // d0 (256^3)
         } else {
 #pragma unroll
             for (int i = 0; i < 4; ++i)  // digit 3 - i: byte i of both elements
-                *reinterpret_cast<uint16_t*>(gp + (3 - i) * 16) =
+                *reinterpret_cast<uint16_t*>(gp + ent(3 - i)) =
                     static_cast<uint16_t>(__byte_perm(e[0], e[1 % NB], i | ((4 + i) << 4)));
         }
     }
@@ -168,7 +175,7 @@ __device__ __forceinline__ void tok_encode(const EncTask<EPT>& r, bool valid, in
 template <int DT, int EPT>
 __device__ void tok_digitize(const uint16_t* __restrict__ src, int v0, int nvec, int Kd, unsigned char* __restrict__ B,
                              float2* __restrict__ fs, int tt, int nthr) {
-    constexpr int NT = 3;
+    constexpr int NT = 2;
     const int total = nvec * Kd / EPT, first = v0 * Kd / EPT;
     const int lane = tt & 31;
     for (int base0 = tt & ~31; base0 < total; base0 += NT * nthr) {
@@ -388,7 +395,8 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
     // lanes whose column group is not their A group hold zeros) and the
     // factors of the lane's groups 8c + 4 (t >> 1) + s, s = 0..3.
     const bool bact = (g >> 2) == (t >> 1);
-    const int bl = (t >> 1) * 8 + (t & 1) * 4 + (g & 3);
+    const int bl = (t >> 1) * 8 + (t & 1) * 4 + (g & 3);  // the lane's entry L, before the swizzle
+    const bool bswap = t >> 1;                             // L >= 8: halves stored swapped
     uint2 bf[4][4];
     float2 fsl[4];
     auto load_b = [&](const unsigned char* col, const float2* fsg) {
@@ -397,9 +405,10 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
 #pragma unroll
             for (int pp = 0; pp < 2; ++pp) {
                 uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                if (bact) v = *reinterpret_cast<const uint4*>(col + s * 512 + pp * 256 + bl * 16);
-                bf[s][2 * pp] = make_uint2(v.x, v.y);
-                bf[s][2 * pp + 1] = make_uint2(v.z, v.w);
+                if (bact) v = *reinterpret_cast<const uint4*>(col + s * 512 + pp * 256 + (((bl & 8) | ((bl & 7) ^ s)) * 16));
+                const uint2 lo = make_uint2(v.x, v.y), hi2 = make_uint2(v.z, v.w);
+                bf[s][2 * pp] = bswap ? hi2 : lo;
+                bf[s][2 * pp + 1] = bswap ? lo : hi2;
             }
         const float4 f0 = *reinterpret_cast<const float4*>(fsg + 4 * (t >> 1));
         const float4 f1 = *reinterpret_cast<const float4*>(fsg + 4 * (t >> 1) + 2);
