@@ -646,7 +646,8 @@ bool up_tile_map(const void* ptr, long long E, int I, int H, CUtensorMap* out) {
 // weights by TMA (token.cu); kNotApplicable when the shapes, the alignment or
 // the shared memory do not fit (gs 64, K <= 8, H <= 4096, H and I multiples
 // of 512, E <= 512 when routing from logits).
-int run_token_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, cudaStream_t st) {
+int run_token_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, cudaStream_t st,
+                    bool status_merge = false) {
     if (c.M != 1 || gs != 64 || c.K > kTokMaxK || c.K < 1 || (c.logits && c.E > kTokMaxE) || c.H % 512 ||
         c.I % 512 || c.H > 4096)
         return kNotApplicable;
@@ -686,6 +687,7 @@ int run_token_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, 
     a.E = c.E;
     a.K = c.K;
     a.spin_limit = spin_limit();
+    a.status_merge = status_merge ? 1 : 0;
     a.rows_per_cta = rpc;
     a.clamp = c.clamp;
     // shared memory (from a 1024-aligned base): the stage ring, the logits,
@@ -759,13 +761,56 @@ int m1_engine() {
     return v;
 }
 
+// Batches of 2..8 tokens: MOMIJ_DECODE_MROW=seq launches the streaming kernel
+// once per token, =tc takes the batched tcgen05 kernel; the default is the
+// token-by-token launches up to kMrowSeqMax tokens (faster as measured here:
+// each token streams its own experts at the streaming kernel's rate, while
+// the batched kernel streams the distinct experts once at a lower rate).
+constexpr int kMrowSeqMax = 8;
+bool mrow_sequential(int M) {
+    static const int v = [] {
+        const char* e = std::getenv("MOMIJ_DECODE_MROW");
+        if (e && std::strcmp(e, "tc") == 0) return 0;
+        if (e && std::strcmp(e, "seq") == 0) return 2;
+        return 1;
+    }();
+    return v == 2 || (v == 1 && M <= kMrowSeqMax);
+}
+
+// The tokens of a batch one by one through the streaming kernel: the same
+// bits as M single-token calls.  kNotApplicable (before any launch) when the
+// kernel does not take the shapes.
+int run_token_batch(const LayerCall& c, int dtype, int gs, const Workspace& ws, cudaStream_t st) {
+    const size_t esz = 2;  // bytes of a 16-bit activation
+    for (int m = 0; m < c.M; ++m) {
+        LayerCall t = c;
+        t.M = 1;
+        t.logits = c.logits ? c.logits + (size_t)m * c.E : nullptr;
+        t.inds_in = c.inds_in ? c.inds_in + (size_t)m * c.K : nullptr;
+        t.scores_in = c.scores_in ? c.scores_in + (size_t)m * c.K : nullptr;
+        t.inds_out = c.inds_out ? c.inds_out + (size_t)m * c.K : nullptr;
+        t.scores_out = c.scores_out ? c.scores_out + (size_t)m * c.K : nullptr;
+        t.x = static_cast<const unsigned char*>(c.x) + (size_t)m * c.H * esz;
+        t.y = c.y ? static_cast<unsigned char*>(c.y) + (size_t)m * c.H * esz : nullptr;
+        t.resid_h = c.resid_h ? static_cast<unsigned char*>(c.resid_h) + (size_t)m * c.H * esz : nullptr;
+        const int rc = run_token_layer(t, dtype, gs, ws, st, m > 0);
+        if (rc != MOMIJ_OK) return rc;  // kNotApplicable only at m == 0: the shapes are the same for every token
+    }
+    return MOMIJ_OK;
+}
+
 // The fused layer: one token on the streaming kernel (or the engine the
-// environment selects), 2..8 tokens on the tcgen05 kernel; kNotApplicable
-// lets the caller fall back to the multi-kernel path.
+// environment selects), 2..8 tokens token by token on the same kernel or on
+// the batched tcgen05 kernel; kNotApplicable lets the caller fall back to the
+// multi-kernel path.
 int run_fused_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, cudaStream_t st) {
     if (!fused_enabled()) return kNotApplicable;
     if (c.M == 1 && m1_engine() == 0) {
         const int rc = run_token_layer(c, dtype, gs, ws, st);
+        if (rc != kNotApplicable) return rc;
+    }
+    if (c.M > 1 && c.M <= 8 && m1_engine() == 0 && mrow_sequential(c.M)) {
+        const int rc = run_token_batch(c, dtype, gs, ws, st);
         if (rc != kNotApplicable) return rc;
     }
     if (c.M == 1 && m1_engine() != 2) {

@@ -287,8 +287,8 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
             bad = e < 0 || e >= E;
         }
         flag = __syncthreads_or(bad);
-        if (bx == 0 && tid == 0)
-            a.ctrl[kCtrlStatus] = flag ? MOMIJ_ERR_EXPERT_INDEX : (s_stop ? MOMIJ_ERR_STOPPED : MOMIJ_OK);
+        const int st0 = flag ? MOMIJ_ERR_EXPERT_INDEX : (s_stop ? MOMIJ_ERR_STOPPED : MOMIJ_OK);
+        if (bx == 0 && tid == 0 && (!a.status_merge || st0 != MOMIJ_OK)) a.ctrl[kCtrlStatus] = st0;
         if (flag) return;  // uniform: every CTA sees the same indices
     }
     if (a.logits && !flag) {
@@ -320,7 +320,8 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
     }
     __syncthreads();
     const bool stopped = s_stop != 0;
-    if (a.logits && bx == 0 && tid == 0) a.ctrl[kCtrlStatus] = stopped ? MOMIJ_ERR_STOPPED : MOMIJ_OK;
+    if (a.logits && bx == 0 && tid == 0 && (!a.status_merge || stopped))
+        a.ctrl[kCtrlStatus] = stopped ? MOMIJ_ERR_STOPPED : MOMIJ_OK;
     tstamp(a, 2);
 
     // ---- work of this CTA ------------------------------------------------------

@@ -50,6 +50,8 @@ struct TokenArgs {
     long long* trace;        // optional: kTracePointsDec %globaltimer stamps per CTA
     int H, I, E, K;
     int spin_limit;          // polls of a bounded wait before it gives up
+    int status_merge;        // 0: set the call's status word; 1: only record a non-OK status (a later
+                             // token of a batch launched token by token)
     int rows_per_cta;        // output rows of a CTA in the down phase (<= kTokDnRows)
     float clamp;
     // dynamic shared-memory carve-up (byte offsets from the 1024-aligned base)
