@@ -751,14 +751,11 @@ int run_token_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, 
 // engine (layer.cu), =tc the tcgen05 kernel (decode.cu); the default is the
 // TMA-streaming kernel (token.cu), with the warp-level engine for the shapes
 // it does not take.
-int m1_engine() {
-    static const int v = [] {
-        const char* e = std::getenv("MOMIJ_DECODE_M1");
-        if (e && std::strcmp(e, "tc") == 0) return 2;
-        if (e && std::strcmp(e, "warp") == 0) return 1;
-        return 0;
-    }();
-    return v;
+int m1_engine() {  // read per call: tests and benchmarks switch engines within a process
+    const char* e = std::getenv("MOMIJ_DECODE_M1");
+    if (e && std::strcmp(e, "tc") == 0) return 2;
+    if (e && std::strcmp(e, "warp") == 0) return 1;
+    return 0;
 }
 
 // Batches of 2..8 tokens: MOMIJ_DECODE_MROW=seq launches the streaming kernel
@@ -767,14 +764,11 @@ int m1_engine() {
 // each token streams its own experts at the streaming kernel's rate, while
 // the batched kernel streams the distinct experts once at a lower rate).
 constexpr int kMrowSeqMax = 8;
-bool mrow_sequential(int M) {
-    static const int v = [] {
-        const char* e = std::getenv("MOMIJ_DECODE_MROW");
-        if (e && std::strcmp(e, "tc") == 0) return 0;
-        if (e && std::strcmp(e, "seq") == 0) return 2;
-        return 1;
-    }();
-    return v == 2 || (v == 1 && M <= kMrowSeqMax);
+bool mrow_sequential(int M) {  // read per call, like m1_engine
+    const char* e = std::getenv("MOMIJ_DECODE_MROW");
+    if (e && std::strcmp(e, "tc") == 0) return false;
+    if (e && std::strcmp(e, "seq") == 0) return true;
+    return M <= kMrowSeqMax;
 }
 
 // The tokens of a batch one by one through the streaming kernel: the same

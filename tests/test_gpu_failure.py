@@ -53,8 +53,12 @@ def _rel(y, ref):
     return float((np.sqrt(((g - r) ** 2).sum(axis=1)) / np.sqrt((r ** 2).sum(axis=1))).max())
 
 
-@pytest.mark.parametrize("M", [1, 2])  # the single-token engine and the tcgen05 kernel
-def test_wait_timeout_is_reported_and_the_workspace_stays_usable(M):
+@pytest.mark.parametrize("M,engine", [(1, None), (2, None), (2, "tc")])
+def test_wait_timeout_is_reported_and_the_workspace_stays_usable(M, engine, monkeypatch):
+    """The streaming single-token kernel (one token, and a batch launched
+    token by token) and the batched tcgen05 kernel."""
+    if engine:
+        monkeypatch.setenv("MOMIJ_DECODE_MROW", engine)
     L = _layer(M=M)
     ws = moe.new_workspace(L["M"], L["K"], L["H"], L["I"])
     try:

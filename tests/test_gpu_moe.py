@@ -293,18 +293,19 @@ def test_fused_expert_matches_oracle(M, H, I, E, K, gs, dt):
     (5, 4096, 256, 32, 8, 64, 0, None),
 ])
 def test_fused_layer_and_multikernel_path_match_oracle(M, H, I, E, K, gs, dt, rho, monkeypatch):
-    """The one-kernel decode layer (route + up + grid barrier + down +
-    last-arriver combine on the tcgen05 tensor cores) and the multi-kernel
-    path (route/plan, up, down, combine kernels on the GEMV engine) both match
-    the oracle, call after call on one workspace (the grid-barrier and
-    completion counters return to zero); repeated calls of the fused layer
-    give the same bits."""
+    """The one-kernel decode layers (the streaming single-token kernel, also
+    token by token for a batch, and the batched tcgen05 kernel) and the
+    multi-kernel path (route/plan, up, down, combine kernels on the GEMV
+    engine) all match the oracle, call after call on one workspace (the
+    grid-barrier and completion counters return to zero); repeated calls of
+    the fused layer give the same bits."""
     w = S.expert_weights(E, H, I, gs, seed=13, dtype=dt)
     dw = dev_weights(w, dt)
     ws = moe.new_workspace(M, K, H, I)
     outs = {}
-    for path in ("1", "0"):
-        monkeypatch.setenv("MOMIJ_FUSED", path)
+    for path in ("1", "tc", "0"):  # fused (token kernel; token by token for M > 1), batched tcgen05, multi-kernel
+        monkeypatch.setenv("MOMIJ_FUSED", "0" if path == "0" else "1")
+        monkeypatch.setenv("MOMIJ_DECODE_MROW", "tc" if path == "tc" else "auto")
         for call in range(4):
             lay = call % 2  # calls 2 and 3 repeat the inputs of calls 0 and 1
             x = S.activations(M, H, layer=lay, seed=13, dtype=dt)
@@ -326,9 +327,10 @@ def test_fused_layer_and_multikernel_path_match_oracle(M, H, I, E, K, gs, dt, rh
             assert (outs[(path, call)][2] == i_ref).all()
             assert_ffn_parity(outs[(path, call)][0], y_ref, st["down"], s_ref, dt, f"path {path} call {call}")
             assert_ffn_parity(outs[(path, call)][1], h_ref, st["down"], s_ref, dt, f"path {path} call {call} resid")
-    for call in (2, 3):
-        for a, b in zip(outs[("1", call)], outs[("1", call - 2)]):
-            assert (a == b).all(), call
+    for path in ("1", "tc"):
+        for call in (2, 3):
+            for a, b in zip(outs[(path, call)], outs[(path, call - 2)]):
+                assert (a == b).all(), (path, call)
 
 
 def test_fused_expert_mrow_matches_sequential():
