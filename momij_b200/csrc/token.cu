@@ -539,6 +539,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
     // ---- 4. down phase: the K act vectors encoded, then warp 2k + q takes
     // expert slot k's 16-row half q
     if (fine && nrows > 0) tok_digitize<DT, 16>(a.act, 0, K, I, s_ab, s_afs, tid, kTokCompute);
+    tstamp(a, 9);
     bar_sync(1, kTokCompute);
     if (nrows > 0) {
         const int k = warp >> 1, q = warp & 1;
