@@ -558,7 +558,20 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
                 const uint2 sv = *reinterpret_cast<const uint2*>(st + kTokSOff + so);
                 const uint2 bv = *reinterpret_cast<const uint2*>(st + kTokBOff + so);
                 const float v = compute(st + k * 4096 + q * 2048, 1024, sv, bv);
-                if (t < 2) s_red_dn[(k * kTokDnRows + 16 * q + g + 8 * t) * RSD + c] = v;
+                const int r = 16 * q + g + 8 * t;
+                if (t < 2) {
+                    if (c + 1 < ncol_dn) {
+                        s_red_dn[(k * kTokDnRows + r) * RSD + c] = v;
+                    } else {
+                        // the last column: the expert's down value of the row, summed over
+                        // the columns in order and rounded like a gather output
+                        const float* rd = s_red_dn + (k * kTokDnRows + r) * RSD;
+                        float dv = 0.f;
+                        for (int cc = 0; cc < c; ++cc) dv += rd[cc];
+                        dv += v;
+                        if (r < nrows) s_dv[r * kTokMaxK + k] = Half<DT>::to_f(Half<DT>::from_f(dv));
+                    }
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_empty[slot]);
@@ -571,16 +584,6 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
 
     // ---- 5. combine of the CTA's rows ----------------------------------------------
     if (fine && !s_abort && nrows > 0) {
-        {
-            const int r = tid >> 3, k = tid & 7;  // (row, expert slot)
-            if (r < nrows && k < K) {
-                const float* rd = s_red_dn + (k * kTokDnRows + r) * RSD;
-                float dv = 0.f;
-                for (int c = 0; c < ncol_dn; ++c) dv += rd[c];
-                s_dv[r * kTokMaxK + k] = Half<DT>::to_f(Half<DT>::from_f(dv));
-            }
-        }
-        bar_sync(1, kTokCompute);
         if (tid < nrows) {
             float acc = 0.f;
             for (int k = 0; k < K; ++k) acc = fmaf(s_dv[tid * kTokMaxK + k], s_scores[k], acc);
