@@ -271,6 +271,8 @@ def test_up_swiglu_matches_oracle(M, H, I, E, K, gs, dt):
     (1, 2048, 1024, 64, 4, 64, 0),   # BASELINE config 0 shapes
     (4, 1024, 512, 16, 4, 64, 0),
     (2, 512, 768, 12, 3, 128, 1),
+    (1, 1024, 512, 16, 4, 64, 1),    # fp16 on the streaming single-token kernel
+    (3, 2048, 1024, 32, 8, 64, 1),   # fp16, token by token, K = 8
 ])
 def test_fused_expert_matches_oracle(M, H, I, E, K, gs, dt):
     w = S.expert_weights(E, H, I, gs, seed=9, dtype=dt)
