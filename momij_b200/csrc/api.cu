@@ -648,8 +648,8 @@ bool up_tile_map(const void* ptr, long long E, int I, int H, CUtensorMap* out) {
 // of 512, E <= 512 when routing from logits).
 int run_token_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, cudaStream_t st,
                     bool status_merge = false) {
-    if (c.M != 1 || gs != 64 || c.K > kTokMaxK || c.K < 1 || (c.logits && c.E > kTokMaxE) || c.H % 512 ||
-        c.I % 512 || c.H > 4096)
+    if (c.M < 1 || c.M > kTokMaxM || gs != 64 || c.K > kTokMaxK || c.K < 1 || (c.logits && c.E > kTokMaxE) ||
+        c.H % 512 || c.I % 512 || c.H > 4096)
         return kNotApplicable;
     if (!aligned(c.w_ug, 16) || !aligned(c.w_dn, 16) || !aligned(c.s_ug, 16) || !aligned(c.b_ug, 16) ||
         !aligned(c.s_dn, 16) || !aligned(c.b_dn, 16) || !aligned(c.x, 16) || !aligned(ws.act, 16))
@@ -686,6 +686,7 @@ int run_token_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, 
     a.I = c.I;
     a.E = c.E;
     a.K = c.K;
+    a.M = c.M;
     a.spin_limit = spin_limit();
     a.status_merge = status_merge ? 1 : 0;
     a.rows_per_cta = rpc;
@@ -697,7 +698,7 @@ int run_token_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, 
     a.off_ring = (int)off;
     off += (size_t)kTokStages * kTokStageBytes;
     a.off_logits = (int)off;
-    off = align_up(off + 4 * (size_t)kTokThreads, 128);
+    off = align_up(off + 4 * std::max((size_t)kTokThreads, (size_t)c.M * c.E), 128);
     const size_t reg = off;
     a.off_xb = (int)off;
     off = align_up(off + tok_b_bytes(c.H), 16);
@@ -758,17 +759,19 @@ int m1_engine() {  // read per call: tests and benchmarks switch engines within 
     return 0;
 }
 
-// Batches of 2..8 tokens: MOMIJ_DECODE_MROW=seq launches the streaming kernel
-// once per token, =tc takes the batched tcgen05 kernel; the default is the
-// token-by-token launches up to kMrowSeqMax tokens (faster as measured here:
-// each token streams its own experts at the streaming kernel's rate, while
-// the batched kernel streams the distinct experts once at a lower rate).
-constexpr int kMrowSeqMax = 8;
-bool mrow_sequential(int M) {  // read per call, like m1_engine
+// Batches of 2..8 tokens: by default one launch of the streaming kernel that
+// takes the tokens one after another (its producer streams the next token's
+// weights during the current token's serial tail); MOMIJ_DECODE_MROW=seq
+// launches it once per token, =tc takes the batched tcgen05 kernel.  Both
+// streaming forms give the bits of M single-token calls; they beat the
+// batched kernel at every size measured here (each token streams its own
+// experts at the streaming rate, the batched kernel the distinct experts
+// once at a lower rate).  Read per call, like m1_engine.
+int mrow_mode() {
     const char* e = std::getenv("MOMIJ_DECODE_MROW");
-    if (e && std::strcmp(e, "tc") == 0) return false;
-    if (e && std::strcmp(e, "seq") == 0) return true;
-    return M <= kMrowSeqMax;
+    if (e && std::strcmp(e, "tc") == 0) return 2;
+    if (e && std::strcmp(e, "seq") == 0) return 1;
+    return 0;
 }
 
 // The tokens of a batch one by one through the streaming kernel: the same
@@ -803,9 +806,11 @@ int run_fused_layer(const LayerCall& c, int dtype, int gs, const Workspace& ws, 
         const int rc = run_token_layer(c, dtype, gs, ws, st);
         if (rc != kNotApplicable) return rc;
     }
-    if (c.M > 1 && c.M <= 8 && m1_engine() == 0 && mrow_sequential(c.M)) {
-        const int rc = run_token_batch(c, dtype, gs, ws, st);
+    if (c.M > 1 && c.M <= kTokMaxM && m1_engine() == 0 && mrow_mode() != 2) {
+        const int rc = mrow_mode() == 0 ? run_token_layer(c, dtype, gs, ws, st) : kNotApplicable;
         if (rc != kNotApplicable) return rc;
+        const int rs = run_token_batch(c, dtype, gs, ws, st);
+        if (rs != kNotApplicable) return rs;
     }
     if (c.M == 1 && m1_engine() != 2) {
         const int rc = run_layer_engine(c, dtype, gs, ws, st);

@@ -230,11 +230,11 @@ template <int DT>
 __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_constant__ TokenArgs a) {
     extern __shared__ unsigned char smem_raw[];
     __shared__ __align__(8) uint64_t s_full[kTokStages], s_empty[kTokStages];
-    __shared__ int s_inds[kTokMaxK];
-    __shared__ float s_scores[kTokMaxK];
+    __shared__ int s_inds[kTokMaxM * kTokMaxK];      // token m's experts at m * K
+    __shared__ float s_scores[kTokMaxM * kTokMaxK];
     __shared__ float s_part[kTokWarps];
     __shared__ float s_max;
-    __shared__ int s_nan[1];
+    __shared__ int s_nan[kTokMaxM];
     __shared__ int s_stop, s_flag;
     __shared__ volatile int s_abort, s_never;
     __shared__ float s_dv[kTokDnRows * kTokMaxK];
@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, t = lane & 3;
     const int G = gridDim.x, bx = blockIdx.x;
-    const int H = a.H, I = a.I, E = a.E, K = a.K;
+    const int H = a.H, I = a.I, E = a.E, K = a.K, M = a.M;
     unsigned char* smem =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     unsigned char* s_ring = smem + a.off_ring;
@@ -273,14 +273,29 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
     EncTask<8> xraw;
     if (tid < xtasks) tok_load_task<8>(a.x, H, tid, xraw);
     if (tid == 0) s_stop = a.stop ? __ldcg(a.stop) : 0;
-    const float lc = (a.logits && tid < E) ? __ldcg(a.logits + tid) : -INFINITY;
+    // one token: each thread holds one logit and the routing below ranks them
+    // (its fast path); several: the logits go to shared memory and route_tokens
+    // routes every token (with its scores)
+    const float lc = (a.logits && M == 1 && tid < E) ? __ldcg(a.logits + tid) : -INFINITY;
     int flag;  // a NaN logit (routing from logits) or an expert index out of range (given indices)
-    if (a.logits) {
+    if (a.logits && M == 1) {
         s_logits[tid] = lc;  // E <= kTokThreads
         flag = __syncthreads_or(tid < E && isnan(lc));
+    } else if (a.logits) {
+        for (int i = tid; i < M * E; i += kTokThreads) s_logits[i] = __ldcg(a.logits + i);
+        __syncthreads();
+        if (warp < M) {
+            int nan = 0;
+            for (int e = lane; e < E; e += 32) nan |= isnan(s_logits[warp * E + e]);
+            nan = __any_sync(0xffffffffu, nan);
+            if (lane == 0) s_nan[warp] = nan;
+        }
+        __syncthreads();
+        route_tokens(s_logits, s_nan, M, E, K, 0, kTokThreads, 1, s_inds, s_scores, nullptr, true);
+        flag = 1;  // not the one-token fast path
     } else {
         int bad = 0;
-        if (tid < K) {
+        if (tid < M * K) {
             const int e = a.inds_in[tid];
             s_inds[tid] = e;
             s_scores[tid] = a.scores_in[tid];
@@ -291,7 +306,8 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
         if (bx == 0 && tid == 0 && (!a.status_merge || st0 != MOMIJ_OK)) a.ctrl[kCtrlStatus] = st0;
         if (flag) return;  // uniform: every CTA sees the same indices
     }
-    if (a.logits && !flag) {
+    const bool fast = a.logits && M == 1 && !flag;  // one token routed by the ranking below
+    if (fast) {
         // rank of candidate c over the P threads that share it: the number of
         // experts before it in value order, ties by the smaller bit-reversed index
         int P = 1;
@@ -313,7 +329,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
             s_inds[r] = c;
             if (r == 0) s_max = lv;
         }
-    } else if (a.logits) {
+    } else if (a.logits && M == 1) {
         if (tid == 0) s_nan[0] = 1;
         __syncthreads();
         route_tokens(s_logits, s_nan, 1, E, K, 0, kTokThreads, 1, s_inds, s_scores, nullptr, false);
@@ -333,7 +349,8 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
     const int ncol_up = H >> 9, ncol_dn = I >> 9;  // 128-byte code columns per row
     const int srb_up = H / 32;                     // scale bytes per up||gate row (gs 64)
     const int n_up_st = (ntiles + 1) >> 1;
-    const int n_st = n_up_st + (nrows > 0 ? ncol_dn : 0);
+    const int n_st_tok = n_up_st + (nrows > 0 ? ncol_dn : 0);  // stages per token
+    const int n_st = M * n_st_tok;
     const int RSU = tok_red_stride(ncol_up), RSD = tok_red_stride(ncol_dn);
 
     if (warp >= kTokWarps) {
@@ -349,21 +366,23 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
                     break;
                 }
                 const uint32_t st = smem_u32(s_ring + (size_t)slot * kTokStageBytes);
-                if (j < n_up_st) {
-                    const int nt = min(2, ntiles - 2 * j);
+                const int m = j / n_st_tok, jj = j - m * n_st_tok;  // token, its stage
+                const int* inds = s_inds + m * K;
+                if (jj < n_up_st) {
+                    const int nt = min(2, ntiles - 2 * jj);
                     mbar_expect_tx(&s_full[slot], (uint32_t)(nt * (ncol_up * 2048 + 2 * 16 * srb_up)));
                     for (int q = 0; q < nt; ++q) {
-                        const int gt = tl0 + 2 * j + q, k = gt / tpe, i0 = (gt - k * tpe) * 8;
-                        const int z = 2 * s_inds[k];
+                        const int gt = tl0 + 2 * jj + q, k = gt / tpe, i0 = (gt - k * tpe) * 8;
+                        const int z = 2 * inds[k];
                         tma_load_4d(st + q * 16384, &a.map[0], 0, i0, 0, z, &s_full[slot]);
                         tma_load_3d(st + kTokSOff + q * 2048, &a.map[1], 0, i0, z, &s_full[slot]);
                         tma_load_3d(st + kTokBOff + q * 2048, &a.map[2], 0, i0, z, &s_full[slot]);
                     }
                 } else {
-                    const int c = j - n_up_st;
+                    const int c = jj - n_up_st;
                     mbar_expect_tx(&s_full[slot], (uint32_t)(K * rpc * (128 + 2 * 16)));
                     for (int k = 0; k < K; ++k) {
-                        const int y = s_inds[k] * H + n0;
+                        const int y = inds[k] * H + n0;
                         tma_load_2d(st + k * 4096, &a.map[3], c * 128, y, &s_full[slot]);
                         tma_load_2d(st + kTokSOff + k * 512, &a.map[4], c * 16, y, &s_full[slot]);
                         tma_load_2d(st + kTokBOff + k * 512, &a.map[5], c * 16, y, &s_full[slot]);
@@ -379,224 +398,236 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
     }
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kTokRegsCompute));
 
-    // ---- token encoding and scores while the first stages land -----------------------
-    if (tid < ((xtasks + 31) & ~31)) tok_encode<DT, 8>(xraw, tid < xtasks, min(tid, xtasks - 1), H, s_xb, s_xfs);
-    if (a.logits && !flag) {
-        // softmax denominator over all experts (max = the top-ranked logit);
-        // the renormalised scores follow after the up||gate phase
-        float ez = tid < E ? expf(lc - s_max) : 0.f;
+    // ---- the tokens one after another; the producer streams ahead across them ---------
+    bool any_fail = false;  // a wait gave up or a grid barrier did not complete
+#pragma unroll 1
+    for (int m = 0; m < M; ++m) {
+        const int* inds_m = s_inds + m * K;
+        float* scores_m = s_scores + m * K;
+        const int jm = m * n_st_tok;  // the token's first stage
+        // ---- token encoding (and the one-token scores) while its first stages land ------
+        if (tid < ((xtasks + 31) & ~31)) tok_encode<DT, 8>(xraw, tid < xtasks, min(tid, xtasks - 1), H, s_xb, s_xfs);
+        if (fast) {
+            // softmax denominator over all experts (max = the top-ranked logit);
+            // the renormalised scores follow after the up||gate phase
+            float ez = tid < E ? expf(lc - s_max) : 0.f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ez += __shfl_xor_sync(0xffffffffu, ez, o);
-        if (lane == 0) s_part[warp] = ez;
-    }
-    bar_sync(1, kTokCompute);
-    tstamp(a, 3);
-
-    // Digit operand fragments of a code column (bf[slab][class] = (b0, b1);
-    // lanes whose column group is not their A group hold zeros) and the
-    // factors of the lane's groups 8c + 4 (t >> 1) + s, s = 0..3.
-    const bool bact = (g >> 2) == (t >> 1);
-    const int bl = (t >> 1) * 8 + (t & 1) * 4 + (g & 3);  // the lane's entry L, before the swizzle
-    const bool bswap = t >> 1;                             // L >= 8: halves stored swapped
-    uint2 bf[4][4];
-    float2 fsl[4];
-    auto load_b = [&](const unsigned char* col, const float2* fsg) {
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-#pragma unroll
-            for (int pp = 0; pp < 2; ++pp) {
-                uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                if (bact) v = *reinterpret_cast<const uint4*>(col + s * 512 + pp * 256 + (((bl & 8) | ((bl & 7) ^ s)) * 16));
-                const uint2 lo = make_uint2(v.x, v.y), hi2 = make_uint2(v.z, v.w);
-                bf[s][2 * pp] = bswap ? hi2 : lo;
-                bf[s][2 * pp + 1] = bswap ? lo : hi2;
-            }
-        const float4 f0 = *reinterpret_cast<const float4*>(fsg + 4 * (t >> 1));
-        const float4 f1 = *reinterpret_cast<const float4*>(fsg + 4 * (t >> 1) + 2);
-        fsl[0] = make_float2(f0.x, f0.y);
-        fsl[1] = make_float2(f0.z, f0.w);
-        fsl[2] = make_float2(f1.x, f1.y);
-        fsl[3] = make_float2(f1.z, f1.w);
-    };
-
-    // One 16-row tile of 128-byte swizzled code rows (row r < 8 at cb + 128 r,
-    // row 8 + r at cb + hi + 128 r): rows g (even t) or g + 8 (odd t) of the
-    // lane's four groups, summed as
-    // (G_j0 + .. + G_j3) + (G_j4 + .. + G_j7); `sv`, `bv`: the four scales and
-    // biases of the lane's row and groups.  Lanes t = 0, 1 return rows g, g + 8.
-    const bool odd = t & 1;
-    auto compute = [&](const unsigned char* cb, int hi, uint2 sv, uint2 bv) -> float {
-        uint2 ra[4], rb[4];
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-            const int off = (((s + 4 * (t >> 1)) ^ (g & 7)) << 4) + 8 * (t & 1);
-            ra[s] = *reinterpret_cast<const uint2*>(cb + g * 128 + off);
-            rb[s] = *reinterpret_cast<const uint2*>(cb + hi + g * 128 + off);
+            for (int o = 16; o > 0; o >>= 1) ez += __shfl_xor_sync(0xffffffffu, ez, o);
+            if (lane == 0) s_part[warp] = ez;
         }
-        int acc[4][4];
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
-#pragma unroll
-            for (int r = 0; r < 4; ++r) acc[s][r] = 0;
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-            const uint32_t m = 0x03030303u << (2 * p);
+        bar_sync(1, kTokCompute);
+        tstamp(a, 3);
+
+        // Digit operand fragments of a code column (bf[slab][class] = (b0, b1);
+        // lanes whose column group is not their A group hold zeros) and the
+        // factors of the lane's groups 8c + 4 (t >> 1) + s, s = 0..3.
+        const bool bact = (g >> 2) == (t >> 1);
+        const int bl = (t >> 1) * 8 + (t & 1) * 4 + (g & 3);  // the lane's entry L, before the swizzle
+        const bool bswap = t >> 1;                             // L >= 8: halves stored swapped
+        uint2 bf[4][4];
+        float2 fsl[4];
+        auto load_b = [&](const unsigned char* col, const float2* fsg) {
 #pragma unroll
             for (int s = 0; s < 4; ++s)
-                mma_u8s8(acc[s], ra[s].x & m, rb[s].x & m, ra[s].y & m, rb[s].y & m, bf[s][p].x, bf[s][p].y);
-        }
-        const uint32_t sw[2] = {sv.x, sv.y}, bw[2] = {bv.x, bv.y};
-        float v = 0.f;
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {
-            const int* c = acc[s];
-            const int rx = __shfl_xor_sync(0xffffffffu, odd ? c[0] : c[2], 1);
-            const int ry = __shfl_xor_sync(0xffffffffu, odd ? c[1] : c[3], 1);
-            const int d0 = odd ? rx : c[0], d1 = odd ? ry : c[1];
-            const int d2 = odd ? c[2] : rx, d3 = odd ? c[3] : ry;
-            const float f = fmaf((float)d0, 16777216.f, fmaf((float)d1, 65536.f, (float)(d2 * 256 + d3)));
-            const float sf = Half<DT>::to_f(static_cast<uint16_t>(sw[s >> 1] >> (16 * (s & 1))));
-            const float bb = Half<DT>::to_f(static_cast<uint16_t>(bw[s >> 1] >> (16 * (s & 1))));
-            v += fmaf(sf, f * fsl[s].x, bb * fsl[s].y);
-        }
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        return v;
-    };
-
-    bool okw = true;  // this warp's waits all succeeded
-    // ---- 2. up||gate phase ---------------------------------------------------
-    {
-        const int q = warp >> 3, c = warp & 7;
-        if (c < ncol_up) load_b(s_xb + (size_t)c * 2048, s_xfs + 8 * c);
-        const int row = g + 8 * (t & 1);
-#pragma unroll 1
-        for (int j = 0; j < n_up_st; ++j) {
-            const int slot = j % kTokStages;
-            okw = mbar_wait_bounded(&s_full[slot], (j / kTokStages) & 1, a.spin_limit, &s_abort);
-            if (!okw) break;  // the slot stays held: the producer stops at it
-            const int tau = 2 * j + q;
-            if (c < ncol_up && tau < ntiles) {
-                const unsigned char* st = s_ring + (size_t)slot * kTokStageBytes;
-                const unsigned char* sbr = st + q * 2048 + row * srb_up;
-                const int so = srb_up == 128 ? (((c ^ (row & 7)) << 4) + 8 * (t >> 1)) : (c * 16 + 8 * (t >> 1));
-                const uint2 sv = *reinterpret_cast<const uint2*>(sbr + kTokSOff + so);
-                const uint2 bv = *reinterpret_cast<const uint2*>(sbr + kTokBOff + so);
-                const float v = compute(st + q * 16384 + c * 1024, ncol_up * 1024, sv, bv);
-                if (t < 2) s_red_up[(tau * 16 + g + 8 * t) * RSU + c] = v;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[slot]);
-        }
-    }
-    if (!okw && lane == 0) s_abort = 1;
-    bar_sync(1, kTokCompute);
-    tstamp(a, 4);
-    // staged SwiGLU of each row pair of the slice (code columns summed in order)
-    if (tid < 8 * ntiles && !s_abort) {
-        const int tau = tid >> 3, i = tid & 7;
-        const int gt = tl0 + tau, k = gt / tpe, i0 = (gt - k * tpe) * 8;
-        const float* ru = s_red_up + (tau * 16 + i) * RSU;
-        const float* rg = ru + 8 * RSU;
-        float up = 0.f, gate = 0.f;
-        for (int c = 0; c < ncol_up; ++c) {
-            up += ru[c];
-            gate += rg[c];
-        }
-        a.act[(size_t)k * I + i0 + i] = swiglu_staged<DT>(up, gate, a.clamp);
-    }
-    if (a.logits && warp == kTokWarps - 1) {
-        if (!flag) {
-            // the selected gates renormalised by their sum in k order
-            float z = 0.f;
-            for (int w = 0; w < kTokWarps; ++w) z += s_part[w];
-            const float gate = lane < K ? expf(s_logits[s_inds[lane]] - s_max) / z : 0.f;
-            float sum = 0.f;
-            for (int k = 0; k < K; ++k) sum += __shfl_sync(0xffffffffu, gate, k);
-            if (lane < K) s_scores[lane] = gate / sum;
-        } else {
-            route_scores_warp(s_logits, E, K, s_inds, s_scores);
-        }
-    }
-    // the residual rows this CTA updates at the end, in flight meanwhile
-    const uint16_t hres = (a.h && tid < nrows) ? a.h[n0 + tid] : (uint16_t)0;
-
-    // ---- 3. grid barrier ------------------------------------------------------------
-    bar_sync(1, kTokCompute);
-    if (bx == 0 && tid < K) {
-        if (a.inds_out) a.inds_out[tid] = s_inds[tid];
-        if (a.scores_out) a.scores_out[tid] = s_scores[tid];
-    }
-    tstamp(a, 5);
-    if (tid == 0) {
-        const bool okb = tok_grid_barrier(a.bar64, a.spin_limit);
-        if (!okb) s_abort = 1;
-        s_flag = okb;
-    }
-    bar_sync(1, kTokCompute);
-    const bool fine = s_flag != 0 && !s_abort;
-    tstamp(a, 6);
-
-    // ---- 4. down phase: the K act vectors encoded, then warp 2k + q takes
-    // expert slot k's 16-row half q
-    if (fine && nrows > 0) tok_digitize<DT, 16>(a.act, 0, K, I, s_ab, s_afs, tid, kTokCompute);
-    tstamp(a, 9);
-    bar_sync(1, kTokCompute);
-    if (nrows > 0) {
-        const int k = warp >> 1, q = warp & 1;
-        const int row = g + 8 * (t & 1);
-        const bool mine = k < K && 16 * q < nrows;
-        okw = true;
-#pragma unroll 1
-        for (int c = 0; c < ncol_dn; ++c) {
-            const int j = n_up_st + c, slot = j % kTokStages;
-            okw = mbar_wait_bounded(&s_full[slot], (j / kTokStages) & 1, a.spin_limit, &s_abort);
-            if (!okw) break;
-            if (fine && mine) {
-                load_b(s_ab + (size_t)k * tok_b_bytes(I) + (size_t)c * 2048, s_afs + (size_t)k * (I >> 6) + 8 * c);
-                const unsigned char* st = s_ring + (size_t)slot * kTokStageBytes;
-                const int so = k * 512 + (16 * q + row) * 16 + 8 * (t >> 1);
-                const uint2 sv = *reinterpret_cast<const uint2*>(st + kTokSOff + so);
-                const uint2 bv = *reinterpret_cast<const uint2*>(st + kTokBOff + so);
-                const float v = compute(st + k * 4096 + q * 2048, 1024, sv, bv);
-                const int r = 16 * q + g + 8 * t;
-                if (t < 2) {
-                    if (c + 1 < ncol_dn) {
-                        s_red_dn[(k * kTokDnRows + r) * RSD + c] = v;
-                    } else {
-                        // the last column: the expert's down value of the row, summed over
-                        // the columns in order and rounded like a gather output
-                        const float* rd = s_red_dn + (k * kTokDnRows + r) * RSD;
-                        float dv = 0.f;
-                        for (int cc = 0; cc < c; ++cc) dv += rd[cc];
-                        dv += v;
-                        if (r < nrows) s_dv[r * kTokMaxK + k] = Half<DT>::to_f(Half<DT>::from_f(dv));
-                    }
+                for (int pp = 0; pp < 2; ++pp) {
+                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                    if (bact) v = *reinterpret_cast<const uint4*>(col + s * 512 + pp * 256 + (((bl & 8) | ((bl & 7) ^ s)) * 16));
+                    const uint2 lo = make_uint2(v.x, v.y), hi2 = make_uint2(v.z, v.w);
+                    bf[s][2 * pp] = bswap ? hi2 : lo;
+                    bf[s][2 * pp + 1] = bswap ? lo : hi2;
                 }
+            const float4 f0 = *reinterpret_cast<const float4*>(fsg + 4 * (t >> 1));
+            const float4 f1 = *reinterpret_cast<const float4*>(fsg + 4 * (t >> 1) + 2);
+            fsl[0] = make_float2(f0.x, f0.y);
+            fsl[1] = make_float2(f0.z, f0.w);
+            fsl[2] = make_float2(f1.x, f1.y);
+            fsl[3] = make_float2(f1.z, f1.w);
+        };
+
+        // One 16-row tile of 128-byte swizzled code rows (row r < 8 at cb + 128 r,
+        // row 8 + r at cb + hi + 128 r): rows g (even t) or g + 8 (odd t) of the
+        // lane's four groups, summed as
+        // (G_j0 + .. + G_j3) + (G_j4 + .. + G_j7); `sv`, `bv`: the four scales and
+        // biases of the lane's row and groups.  Lanes t = 0, 1 return rows g, g + 8.
+        const bool odd = t & 1;
+        auto compute = [&](const unsigned char* cb, int hi, uint2 sv, uint2 bv) -> float {
+            uint2 ra[4], rb[4];
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const int off = (((s + 4 * (t >> 1)) ^ (g & 7)) << 4) + 8 * (t & 1);
+                ra[s] = *reinterpret_cast<const uint2*>(cb + g * 128 + off);
+                rb[s] = *reinterpret_cast<const uint2*>(cb + hi + g * 128 + off);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_empty[slot]);
+            int acc[4][4];
+#pragma unroll
+            for (int s = 0; s < 4; ++s)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) acc[s][r] = 0;
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                const uint32_t m = 0x03030303u << (2 * p);
+#pragma unroll
+                for (int s = 0; s < 4; ++s)
+                    mma_u8s8(acc[s], ra[s].x & m, rb[s].x & m, ra[s].y & m, rb[s].y & m, bf[s][p].x, bf[s][p].y);
+            }
+            const uint32_t sw[2] = {sv.x, sv.y}, bw[2] = {bv.x, bv.y};
+            float v = 0.f;
+#pragma unroll
+            for (int s = 0; s < 4; ++s) {
+                const int* c = acc[s];
+                const int rx = __shfl_xor_sync(0xffffffffu, odd ? c[0] : c[2], 1);
+                const int ry = __shfl_xor_sync(0xffffffffu, odd ? c[1] : c[3], 1);
+                const int d0 = odd ? rx : c[0], d1 = odd ? ry : c[1];
+                const int d2 = odd ? c[2] : rx, d3 = odd ? c[3] : ry;
+                const float f = fmaf((float)d0, 16777216.f, fmaf((float)d1, 65536.f, (float)(d2 * 256 + d3)));
+                const float sf = Half<DT>::to_f(static_cast<uint16_t>(sw[s >> 1] >> (16 * (s & 1))));
+                const float bb = Half<DT>::to_f(static_cast<uint16_t>(bw[s >> 1] >> (16 * (s & 1))));
+                v += fmaf(sf, f * fsl[s].x, bb * fsl[s].y);
+            }
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            return v;
+        };
+
+        bool okw = true;  // this warp's waits all succeeded
+        // ---- 2. up||gate phase ---------------------------------------------------
+        {
+            const int q = warp >> 3, c = warp & 7;
+            if (c < ncol_up) load_b(s_xb + (size_t)c * 2048, s_xfs + 8 * c);
+            const int row = g + 8 * (t & 1);
+#pragma unroll 1
+            for (int jj = 0; jj < n_up_st; ++jj) {
+                const int j = jm + jj, slot = j % kTokStages;
+                okw = mbar_wait_bounded(&s_full[slot], (j / kTokStages) & 1, a.spin_limit, &s_abort);
+                if (!okw) break;  // the slot stays held: the producer stops at it
+                const int tau = 2 * jj + q;
+                if (c < ncol_up && tau < ntiles) {
+                    const unsigned char* st = s_ring + (size_t)slot * kTokStageBytes;
+                    const unsigned char* sbr = st + q * 2048 + row * srb_up;
+                    const int so = srb_up == 128 ? (((c ^ (row & 7)) << 4) + 8 * (t >> 1)) : (c * 16 + 8 * (t >> 1));
+                    const uint2 sv = *reinterpret_cast<const uint2*>(sbr + kTokSOff + so);
+                    const uint2 bv = *reinterpret_cast<const uint2*>(sbr + kTokBOff + so);
+                    const float v = compute(st + q * 16384 + c * 1024, ncol_up * 1024, sv, bv);
+                    if (t < 2) s_red_up[(tau * 16 + g + 8 * t) * RSU + c] = v;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_empty[slot]);
+            }
         }
         if (!okw && lane == 0) s_abort = 1;
-    }
-    bar_sync(1, kTokCompute);
-    tstamp(a, 7);
-    if (tid == 0 && (s_abort || !s_flag)) atomicExch(a.ctrl + kCtrlError, MOMIJ_ERR_TIMEOUT);
-
-    // ---- 5. combine of the CTA's rows ----------------------------------------------
-    if (fine && !s_abort && nrows > 0) {
-        if (tid < nrows) {
-            float acc = 0.f;
-            for (int k = 0; k < K; ++k) acc = fmaf(s_dv[tid * kTokMaxK + k], s_scores[k], acc);
-            const int n = n0 + tid;
-            if (a.h) {
-                const float delta = Half<DT>::to_f(Half<DT>::from_f(acc));
-                a.h[n] = Half<DT>::from_f(Half<DT>::to_f(hres) + delta);
+        bar_sync(1, kTokCompute);
+        tstamp(a, 4);
+        // staged SwiGLU of each row pair of the slice (code columns summed in order)
+        if (tid < 8 * ntiles && !s_abort) {
+            const int tau = tid >> 3, i = tid & 7;
+            const int gt = tl0 + tau, k = gt / tpe, i0 = (gt - k * tpe) * 8;
+            const float* ru = s_red_up + (tau * 16 + i) * RSU;
+            const float* rg = ru + 8 * RSU;
+            float up = 0.f, gate = 0.f;
+            for (int c = 0; c < ncol_up; ++c) {
+                up += ru[c];
+                gate += rg[c];
+            }
+            a.act[((size_t)m * K + k) * I + i0 + i] = swiglu_staged<DT>(up, gate, a.clamp);
+        }
+        if (a.logits && M == 1 && warp == kTokWarps - 1) {
+            if (fast) {
+                // the selected gates renormalised by their sum in k order
+                float z = 0.f;
+                for (int w = 0; w < kTokWarps; ++w) z += s_part[w];
+                const float gate = lane < K ? expf(s_logits[s_inds[lane]] - s_max) / z : 0.f;
+                float sum = 0.f;
+                for (int k = 0; k < K; ++k) sum += __shfl_sync(0xffffffffu, gate, k);
+                if (lane < K) s_scores[lane] = gate / sum;
             } else {
-                a.y[n] = Half<DT>::from_f(acc);
+                route_scores_warp(s_logits, E, K, s_inds, s_scores);
             }
         }
-    }
-    tstamp(a, 8);
+        // the residual rows this CTA updates at the end, in flight meanwhile
+        const uint16_t hres = (a.h && tid < nrows) ? a.h[(size_t)m * H + n0 + tid] : (uint16_t)0;
+
+        // ---- 3. grid barrier ------------------------------------------------------------
+        bar_sync(1, kTokCompute);
+        if (bx == 0 && tid < K) {
+            if (a.inds_out) a.inds_out[m * K + tid] = inds_m[tid];
+            if (a.scores_out) a.scores_out[m * K + tid] = scores_m[tid];
+        }
+        tstamp(a, 5);
+        if (tid == 0) {
+            // every CTA arrives once per token, also after a failure (then without waiting)
+            const bool okb = tok_grid_barrier(a.bar64, s_abort ? 0 : a.spin_limit);
+            if (!okb) s_abort = 1;
+            s_flag = okb;
+        }
+        bar_sync(1, kTokCompute);
+        const bool fine = s_flag != 0 && !s_abort;
+        tstamp(a, 6);
+
+        // ---- 4. down phase: the K act vectors encoded, then warp 2k + q takes
+        // expert slot k's 16-row half q
+        if (fine && nrows > 0) tok_digitize<DT, 16>(a.act + (size_t)m * K * I, 0, K, I, s_ab, s_afs, tid, kTokCompute);
+        tstamp(a, 9);
+        bar_sync(1, kTokCompute);
+        // the next token's elements, in flight during this token's down phase
+        if (m + 1 < M && tid < xtasks) tok_load_task<8>(a.x + (size_t)(m + 1) * H, H, tid, xraw);
+        if (nrows > 0) {
+            const int k = warp >> 1, q = warp & 1;
+            const int row = g + 8 * (t & 1);
+            const bool mine = k < K && 16 * q < nrows;
+            okw = true;
+#pragma unroll 1
+            for (int c = 0; c < ncol_dn; ++c) {
+                const int j = jm + n_up_st + c, slot = j % kTokStages;
+                okw = mbar_wait_bounded(&s_full[slot], (j / kTokStages) & 1, a.spin_limit, &s_abort);
+                if (!okw) break;
+                if (fine && mine) {
+                    load_b(s_ab + (size_t)k * tok_b_bytes(I) + (size_t)c * 2048, s_afs + (size_t)k * (I >> 6) + 8 * c);
+                    const unsigned char* st = s_ring + (size_t)slot * kTokStageBytes;
+                    const int so = k * 512 + (16 * q + row) * 16 + 8 * (t >> 1);
+                    const uint2 sv = *reinterpret_cast<const uint2*>(st + kTokSOff + so);
+                    const uint2 bv = *reinterpret_cast<const uint2*>(st + kTokBOff + so);
+                    const float v = compute(st + k * 4096 + q * 2048, 1024, sv, bv);
+                    const int r = 16 * q + g + 8 * t;
+                    if (t < 2) {
+                        if (c + 1 < ncol_dn) {
+                            s_red_dn[(k * kTokDnRows + r) * RSD + c] = v;
+                        } else {
+                            // the last column: the expert's down value of the row, summed over
+                            // the columns in order and rounded like a gather output
+                            const float* rd = s_red_dn + (k * kTokDnRows + r) * RSD;
+                            float dv = 0.f;
+                            for (int cc = 0; cc < c; ++cc) dv += rd[cc];
+                            dv += v;
+                            if (r < nrows) s_dv[r * kTokMaxK + k] = Half<DT>::to_f(Half<DT>::from_f(dv));
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_empty[slot]);
+            }
+            if (!okw && lane == 0) s_abort = 1;
+        }
+        bar_sync(1, kTokCompute);
+        tstamp(a, 7);
+        any_fail = any_fail || s_abort || !s_flag;
+
+        // ---- 5. combine of the CTA's rows ----------------------------------------------
+        if (fine && !s_abort && nrows > 0) {
+            if (tid < nrows) {
+                float acc = 0.f;
+                for (int k = 0; k < K; ++k) acc = fmaf(s_dv[tid * kTokMaxK + k], scores_m[k], acc);
+                const size_t n = (size_t)m * H + n0 + tid;
+                if (a.h) {
+                    const float delta = Half<DT>::to_f(Half<DT>::from_f(acc));
+                    a.h[n] = Half<DT>::from_f(Half<DT>::to_f(hres) + delta);
+                } else {
+                    a.y[n] = Half<DT>::from_f(acc);
+                }
+            }
+        }
+        tstamp(a, 8);
+    }  // tokens
+    if (tid == 0 && any_fail) atomicExch(a.ctrl + kCtrlError, MOMIJ_ERR_TIMEOUT);
 }
 
 template __global__ void moe_token_kernel<MOMIJ_DTYPE_BF16>(const __grid_constant__ TokenArgs);

@@ -17,6 +17,7 @@ constexpr int kTokStages = 4;                       // ring stages
 constexpr int kTokStageBytes = 40960;               // codes (32 KB) + scales (4 KB) + biases (4 KB)
 constexpr int kTokSOff = 32768, kTokBOff = 36864;   // scale and bias regions of a stage
 constexpr int kTokMaxK = 8;                         // experts per token (a down stage holds all K)
+constexpr int kTokMaxM = 8;                         // tokens per launch (processed one after another)
 constexpr int kTokMaxTiles = 48;                    // up||gate tiles (8 row pairs) per CTA
 constexpr int kTokMaxE = 512;                       // experts ranked by the kernel's own router
 constexpr int kTokDnRows = 32;                      // output rows of a CTA (two 16-row MMA tiles)
@@ -35,27 +36,27 @@ struct TokenArgs {
     // [3] down codes, 2D [E*H, I/4] box (128 B, rows_per_cta rows), 128-byte swizzle;
     // [4], [5] its scales / biases, box (16 B, rows_per_cta rows)
     CUtensorMap map[kTokMaps];
-    const float* logits;     // [E] or nullptr (then inds_in / scores_in)
-    const int32_t* inds_in;  // [K]
+    const float* logits;     // [M, E] or nullptr (then inds_in / scores_in)
+    const int32_t* inds_in;  // [M, K]
     const float* scores_in;
     int32_t* inds_out;       // optional copies of the routing (CTA 0 writes)
     float* scores_out;
-    const uint16_t* x;       // [H]
-    uint16_t* act;           // [K, I] staged SwiGLU output (workspace)
-    uint16_t* y;             // [H] output, or nullptr when h is set
+    const uint16_t* x;       // [M, H]
+    uint16_t* act;           // [M, K, I] staged SwiGLU output (workspace), one slice per token
+    uint16_t* y;             // [M, H] output, or nullptr when h is set
     uint16_t* h;             // residual stream updated in place (may alias x)
     int32_t* ctrl;           // control words (kCtrl*): status, sticky error
     unsigned long long* bar64;  // grid-barrier arrivals: a multiple of the grid size between calls
     const int32_t* stop;     // optional stop flag (non-zero: return MOMIJ_ERR_STOPPED)
     long long* trace;        // optional: kTracePointsDec %globaltimer stamps per CTA
-    int H, I, E, K;
+    int M, H, I, E, K;
     int spin_limit;          // polls of a bounded wait before it gives up
     int status_merge;        // 0: set the call's status word; 1: only record a non-OK status (a later
                              // token of a batch launched token by token)
     int rows_per_cta;        // output rows of a CTA in the down phase (<= kTokDnRows)
     float clamp;
     // dynamic shared-memory carve-up (byte offsets from the 1024-aligned base)
-    int off_ring, off_logits;
+    int off_ring, off_logits;  // logits: max(threads, M * E) floats
     int off_xb, off_xfs, off_red_up;   // up phase: x digits, x group factors, partials
     int off_ab, off_afs, off_red_dn;   // down phase (aliases the up-phase region)
 };
