@@ -459,8 +459,11 @@ def run_gpu(args, cfg) -> None:
         # the whole layer is one kernel, the only launch of the layer in the
         # timed graph: its duration there is ms_per_step / L
         m1 = os.environ.get("MOMIJ_DECODE_M1", "")
+        mrow = os.environ.get("MOMIJ_DECODE_MROW", "")
+        streaming = m1 == "" and (M == 1 or mrow != "tc")
         dom_kernel = ("moe_token_kernel (route + up||gate/SwiGLU + down + combine; TMA-fed stages, "
-                      "u8xs8 mma.sync)" if M == 1 and m1 == "" else
+                      "u8xs8 mma.sync" + ("; the batch's tokens one after another)" if M > 1 else ")")
+                      if streaming else
                       "moe_layer_kernel (route + up||gate/SwiGLU + down + combine, warp-level u8xs8 mma)"
                       if M == 1 and m1 == "warp" else
                       "moe_decode_kernel (route + up||gate/SwiGLU + down + combine, tcgen05)")
@@ -511,7 +514,8 @@ def run_gpu(args, cfg) -> None:
             "dtype": ("bf16 tcgen05 GEMM (weights as hi+lo bf16), f32 accumulate, bf16 I/O"
                       if cfg.get("zipf") else
                       "u8 code classes x s8 activation digits -> s32 (mma.sync m16n8k32), f32 scale/bias "
-                      "epilogue, bf16 I/O" if M == 1 and os.environ.get("MOMIJ_DECODE_M1", "") in ("", "warp") else
+                      "epilogue, bf16 I/O" if (os.environ.get("MOMIJ_DECODE_M1", "") in ("", "warp") and
+                                                (M == 1 or os.environ.get("MOMIJ_DECODE_MROW", "") != "tc")) else
                       "tcgen05.mma kind::i8 (u8 code classes x s8 activation digits -> s32 in TMEM), f32 "
                       "scale/bias epilogue, bf16 I/O"),
             "data": "synthetic (seeded generator, momij_b200/synth.py)",
