@@ -195,16 +195,14 @@ __device__ void tok_digitize(const uint16_t* __restrict__ src, int v0, int nvec,
 }
 
 // Grid barrier by one thread per CTA (after a block barrier whose writes it
-// publishes): a release arrival on a 64-bit counter that is a multiple of the
-// grid size between calls (it starts at zero and every CTA of every call
-// arrives exactly once), then acquire polls until it reaches the next
-// multiple, at most `limit` of them.  One round trip to L2 after the last
-// arrival; the counter cannot wrap.
-__device__ __forceinline__ bool tok_grid_barrier(unsigned long long* ctr, int limit) {
-    unsigned long long old;
-    asm volatile("atom.add.release.gpu.global.u64 %0, [%1], 1;\n" : "=l"(old) : "l"(ctr) : "memory");
-    const unsigned long long target = (old / gridDim.x + 1) * gridDim.x;
-    if (old + 1 == target) return true;
+// publishes) on a 64-bit arrival counter that is a multiple of the grid size
+// between calls (it starts at zero and every CTA of every call arrives once
+// per barrier): a release reduction (no reply to wait for), then acquire
+// polls until the counter reaches `target` -- the value read at the start of
+// the call plus the grid size per barrier so far -- at most `limit` polls.
+// The counter cannot wrap.
+__device__ __forceinline__ bool tok_grid_barrier(unsigned long long* ctr, unsigned long long target, int limit) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], 1;\n" ::"l"(ctr) : "memory");
     for (int it = 0; it < limit; ++it) {
         unsigned long long v;
         asm volatile("ld.acquire.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(ctr) : "memory");
@@ -236,6 +234,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
     __shared__ float s_max;
     __shared__ int s_nan[kTokMaxM];
     __shared__ int s_stop, s_flag;
+    __shared__ unsigned long long s_bar0;
     __shared__ volatile int s_abort, s_never;
     __shared__ float s_dv[kTokDnRows * kTokMaxK];
     tstamp(a, 0);
@@ -273,6 +272,8 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
     EncTask<8> xraw;
     if (tid < xtasks) tok_load_task<8>(a.x, H, tid, xraw);
     if (tid == 0) s_stop = a.stop ? __ldcg(a.stop) : 0;
+    // the barrier count before this call (the previous call on the stream is complete)
+    if (tid == 0) s_bar0 = __ldcg(a.bar64);
     // one token: each thread holds one logit and the routing below ranks them
     // (its fast path); several: the logits go to shared memory and route_tokens
     // routes every token (with its scores)
@@ -555,7 +556,8 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
         tstamp(a, 5);
         if (tid == 0) {
             // every CTA arrives once per token, also after a failure (then without waiting)
-            const bool okb = tok_grid_barrier(a.bar64, s_abort ? 0 : a.spin_limit);
+            const bool okb =
+            tok_grid_barrier(a.bar64, s_bar0 + (unsigned long long)(m + 1) * G, s_abort ? 0 : a.spin_limit);
             if (!okb) s_abort = 1;
             s_flag = okb;
         }
