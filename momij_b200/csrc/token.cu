@@ -25,6 +25,11 @@
 //      score_k) in k order (MapleMoE.swift:76-78), or h[n] = cast(h[n] +
 //      cast(acc)) (maple_score_resid) -- no staging of the down outputs and no
 //      cross-CTA completion counters.
+// A launch may carry up to kTokMaxM tokens (a decode or verify batch): they
+// are routed together, then steps 2-5 run for one token after another (act
+// kept per token, one grid barrier per token) while the producer streams the
+// next token's weights during the current token's serial tail; every token
+// gets the bits of a single-token call.
 //
 // Arithmetic (exact integer inner products on the tensor cores): a 16-code
 // word w gives the u8 operand of code class p (the code at bit offset 2p of
