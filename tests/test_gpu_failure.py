@@ -55,8 +55,8 @@ def _rel(y, ref):
 
 @pytest.mark.parametrize("M,engine", [(1, None), (2, None), (2, "tc")])
 def test_wait_timeout_is_reported_and_the_workspace_stays_usable(M, engine, monkeypatch):
-    """The streaming single-token kernel (one token, and a batch launched
-    token by token) and the batched tcgen05 kernel."""
+    """The streaming kernel (one token, and two tokens in one launch) and
+    the batched tcgen05 kernel."""
     if engine:
         monkeypatch.setenv("MOMIJ_DECODE_MROW", engine)
     L = _layer(M=M)
