@@ -202,16 +202,19 @@ __device__ void tok_digitize(const uint16_t* __restrict__ src, int v0, int nvec,
 // Grid barrier by one thread per CTA (after a block barrier whose writes it
 // publishes) on a 64-bit arrival counter that is a multiple of the grid size
 // between calls (it starts at zero and every CTA of every call arrives once
-// per barrier): a release reduction (no reply to wait for), then acquire
+// per barrier): a release reduction (no reply to wait for), then relaxed
 // polls until the counter reaches `target` -- the value read at the start of
-// the call plus the grid size per barrier so far -- at most `limit` polls.
-// The counter cannot wrap.
+// the call plus the grid size per barrier so far -- at most `limit` polls,
+// and one acquire fence after the poll that saw it.  The counter cannot wrap.
 __device__ __forceinline__ bool tok_grid_barrier(unsigned long long* ctr, unsigned long long target, int limit) {
     asm volatile("red.release.gpu.global.add.u64 [%0], 1;\n" ::"l"(ctr) : "memory");
     for (int it = 0; it < limit; ++it) {
         unsigned long long v;
-        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(ctr) : "memory");
-        if (v >= target) return true;
+        asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];\n" : "=l"(v) : "l"(ctr) : "memory");
+        if (v >= target) {
+            asm volatile("fence.acq_rel.gpu;\n" ::: "memory");  // with the load: an acquire pattern
+            return true;
+        }
     }
     return false;
 }
@@ -266,6 +269,19 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
         mbar_fence_init();
         s_abort = 0;
         s_never = 0;
+    }
+
+    // Before the wait (nothing here reads memory the previous kernel may write):
+    // the tensor maps' descriptors, and the routing inputs pulled into L2 -- a
+    // prefetch only moves lines into L2, the point of coherence, so a later
+    // load still sees whatever the previous kernel writes there.
+    if (warp == kTokWarps) {
+        if (lane < kTokMaps) asm volatile("prefetch.tensormap [%0];" ::"l"(&a.map[lane]) : "memory");
+        const char* rin = a.logits ? reinterpret_cast<const char*>(a.logits) : reinterpret_cast<const char*>(a.inds_in);
+        const int rbytes = a.logits ? M * E * 4 : M * K * 4;
+        for (int o = 128 * lane; o < rbytes; o += 32 * 128)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(rin + o) : "memory");
+        if (!a.logits && lane == 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(a.scores_in) : "memory");
     }
 
     pdl_wait();  // the previous kernel on the stream (e.g. the layer before) is complete
@@ -429,7 +445,7 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
         // factors of the lane's groups 8c + 4 (t >> 1) + s, s = 0..3.
         const bool bact = (g >> 2) == (t >> 1);
         const int bl = (t >> 1) * 8 + (t & 1) * 4 + (g & 3);  // the lane's entry L, before the swizzle
-        const bool bswap = t >> 1;                             // L >= 8: halves stored swapped
+        const int hsw = (t >> 1) * 8;  // L >= 8: the entry's two 8-byte halves stored swapped
         uint2 bf[4][4];
         float2 fsl[4];
         auto load_b = [&](const unsigned char* col, const float2* fsg) {
@@ -437,11 +453,14 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
             for (int s = 0; s < 4; ++s)
 #pragma unroll
                 for (int pp = 0; pp < 2; ++pp) {
-                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                    if (bact) v = *reinterpret_cast<const uint4*>(col + s * 512 + pp * 256 + (((bl & 8) | ((bl & 7) ^ s)) * 16));
-                    const uint2 lo = make_uint2(v.x, v.y), hi2 = make_uint2(v.z, v.w);
-                    bf[s][2 * pp] = bswap ? hi2 : lo;
-                    bf[s][2 * pp + 1] = bswap ? lo : hi2;
+                    uint2 ev = make_uint2(0u, 0u), od = make_uint2(0u, 0u);  // even, odd class
+                    if (bact) {
+                        const unsigned char* en = col + s * 512 + pp * 256 + (((bl & 8) | ((bl & 7) ^ s)) * 16);
+                        ev = *reinterpret_cast<const uint2*>(en + hsw);
+                        od = *reinterpret_cast<const uint2*>(en + (hsw ^ 8));
+                    }
+                    bf[s][2 * pp] = ev;
+                    bf[s][2 * pp + 1] = od;
                 }
             const float4 f0 = *reinterpret_cast<const float4*>(fsg + 4 * (t >> 1));
             const float4 f1 = *reinterpret_cast<const float4*>(fsg + 4 * (t >> 1) + 2);
