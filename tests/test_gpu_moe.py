@@ -271,8 +271,8 @@ def test_up_swiglu_matches_oracle(M, H, I, E, K, gs, dt):
     (1, 2048, 1024, 64, 4, 64, 0),   # BASELINE config 0 shapes
     (4, 1024, 512, 16, 4, 64, 0),
     (2, 512, 768, 12, 3, 128, 1),
-    (1, 1024, 512, 16, 4, 64, 1),    # fp16 on the streaming single-token kernel
-    (3, 2048, 1024, 32, 8, 64, 1),   # fp16, token by token, K = 8
+    (1, 1024, 512, 16, 4, 64, 1),    # fp16 on the streaming kernel
+    (3, 2048, 1024, 32, 8, 64, 1),   # fp16, three tokens in one streaming launch, K = 8
 ])
 def test_fused_expert_matches_oracle(M, H, I, E, K, gs, dt):
     w = S.expert_weights(E, H, I, gs, seed=9, dtype=dt)
@@ -295,8 +295,8 @@ def test_fused_expert_matches_oracle(M, H, I, E, K, gs, dt):
     (5, 4096, 256, 32, 8, 64, 0, None),
 ])
 def test_fused_layer_and_multikernel_path_match_oracle(M, H, I, E, K, gs, dt, rho, monkeypatch):
-    """The one-kernel decode layers (the streaming single-token kernel, also
-    token by token for a batch, and the batched tcgen05 kernel) and the
+    """The one-kernel decode layers (the streaming kernel, one launch for a
+    batch of up to 8 tokens, and the batched tcgen05 kernel) and the
     multi-kernel path (route/plan, up, down, combine kernels on the GEMV
     engine) all match the oracle, call after call on one workspace (the
     grid-barrier and completion counters return to zero); repeated calls of
@@ -305,7 +305,7 @@ def test_fused_layer_and_multikernel_path_match_oracle(M, H, I, E, K, gs, dt, rh
     dw = dev_weights(w, dt)
     ws = moe.new_workspace(M, K, H, I)
     outs = {}
-    for path in ("1", "tc", "0"):  # fused (token kernel; token by token for M > 1), batched tcgen05, multi-kernel
+    for path in ("1", "tc", "0"):  # fused (streaming kernel), batched tcgen05, multi-kernel
         monkeypatch.setenv("MOMIJ_FUSED", "0" if path == "0" else "1")
         monkeypatch.setenv("MOMIJ_DECODE_MROW", "tc" if path == "tc" else "auto")
         for call in range(4):
