@@ -500,12 +500,14 @@ __global__ void __launch_bounds__(kTokThreads, 1) moe_token_kernel(const __grid_
             float v = 0.f;
 #pragma unroll
             for (int s = 0; s < 4; ++s) {
+                // columns 2t, 2t+1 of rows g and g + 8: digits (D0, D1) on even t, (D2, D3) on
+                // odd t; each lane folds its pairs (|D| < 2^20, so 256 D + D' fits), swaps one
+                // with its neighbour and keeps row g (even t) or g + 8 (odd t)
                 const int* c = acc[s];
-                const int rx = __shfl_xor_sync(0xffffffffu, odd ? c[0] : c[2], 1);
-                const int ry = __shfl_xor_sync(0xffffffffu, odd ? c[1] : c[3], 1);
-                const int d0 = odd ? rx : c[0], d1 = odd ? ry : c[1];
-                const int d2 = odd ? c[2] : rx, d3 = odd ? c[3] : ry;
-                const float f = fmaf((float)d0, 16777216.f, fmaf((float)d1, 65536.f, (float)(d2 * 256 + d3)));
+                const int pg = c[0] * 256 + c[1], pg8 = c[2] * 256 + c[3];
+                const int rv = __shfl_xor_sync(0xffffffffu, odd ? pg : pg8, 1);
+                const int dh = odd ? rv : pg, dl = odd ? pg8 : rv;  // 256 D0 + D1, 256 D2 + D3
+                const float f = fmaf((float)dh, 65536.f, (float)dl);
                 const float sf = Half<DT>::to_f(static_cast<uint16_t>(sw[s >> 1] >> (16 * (s & 1))));
                 const float bb = Half<DT>::to_f(static_cast<uint16_t>(bw[s >> 1] >> (16 * (s & 1))));
                 v += fmaf(sf, f * fsl[s].x, bb * fsl[s].y);
