@@ -1,5 +1,6 @@
-// token.cu -- one MoE FFN layer for a single decode token in one persistent
-// kernel (one CTA per SM, launched cooperatively): a producer warpgroup
+// token.cu -- one MoE FFN layer for a decode token (or a batch of up to 8,
+// one token after another) in one persistent kernel (one CTA per SM,
+// launched cooperatively): a producer warpgroup
 // streams the layer's expert weights by TMA into a ring of CTA-wide stages
 // while 16 compute warps multiply them on the tensor cores; every step that
 // is not streaming weights is short and parallel.
@@ -20,7 +21,9 @@
 //   3. grid barrier (act complete; the down weights are already streaming);
 //   4. down phase: the CTA encodes the K act vectors, then warps 2k and
 //      2k + 1 take expert slot k's two 16-row halves; one stage = one
-//      128-byte code column of the CTA's rows for every expert slot;
+//      128-byte code column of the CTA's rows for every expert slot; in the
+//      epilogue the two lanes holding a row's digit columns fold 256 D0 + D1
+//      and 256 D2 + D3 (|D| < 2^20) and exchange one word;
 //   5. the CTA combines its own rows: y[n] = cast(sum_k float(down_k[n]) *
 //      score_k) in k order (MapleMoE.swift:76-78), or h[n] = cast(h[n] +
 //      cast(acc)) (maple_score_resid) -- no staging of the down outputs and no
